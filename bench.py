@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 DSA lightning indexer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+A step is one indexer call (score + top-2048 select) over one batch of the
+workload.  The default workload is benchmark config 1 (B=64 decode rows,
+seq_lens U[4096, 32768], synthetic inputs generated on the device from a
+fixed seed).  Under torchrun (N > 1) every rank runs its own batch of the
+same shape (rows sharded across GPUs, no collective on the data path:
+"scaling": "weak") and the timing is the max over ranks.
+
+value:     index-K GB/s = algorithmic bytes per call x K / device time of K calls
+           (inputs resident in HBM, 3 rotating copies of the inputs so no call
+           reuses L2-resident K pages of the previous one).
+e2e:       the same metric through the drop-in kernel(...) with pinned host
+           inputs: every step copies all input tensors host->device and the
+           output device->host inside the timed region.
+roofline:  the scoring kernel alone: its algorithmic bytes / its mean
+           CUDA-event duration, against the measured HBM copy bandwidth.
+cpu_baseline: the CPU oracle (exact C restatement, all host threads) on a
+           bounded sample of the same batch (rank 0, N = 1 only).
+--impl reference: the CPU implementation of the path (the oracle port) on
+           the host cores, each step a bounded sample of the workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import _lib, kernel, read_status, run  # noqa: E402
+from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import workloads as W  # noqa: E402
+
+METRIC = "index-K HBM GB/s per indexer call (score + top-2048), B=64 decode"
+FALLBACK_HBM_GBS = 6650.0
+N_SETS = 3
+
+
+def measured_hbm_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback 6.65 TB/s"
+
+
+def score_bytes(inp) -> int:
+    """Algorithmic bytes of the scoring kernel: per scored row 132*L (K +
+    scale) + 4*ceil(L/64) (block table) + 8192 (q) + 256 (weights) + 4."""
+    sl = np.clip(inp.seq_lens.cpu().numpy().astype(np.int64), 0, inp.max_pages * 64)
+    sl = sl[sl > 2048]
+    return int((132 * sl + 4 * ((sl + 63) // 64) + 8192 + 256 + 4).sum())
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.lines: list[str] = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            self.sel = str(device.index or 0)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", self.sel], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)  # at least one sample at the end of the region
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def parity_guard(inp) -> None:
+    """Refuses to time a wrong kernel: the selected ids of every row must be
+    distinct, reachable through the block table and an exact top-2048 of the
+    kernel's own logits.  Runs once, outside the timed region, on torch."""
+    out = inp.out()
+    lg = torch.full((inp.rows, inp.max_pages * 64), float("nan"), device=inp.q.device)
+    run(inp.q, inp.k_cache, inp.weights, inp.seq_lens, inp.block_table, out, logits_out=lg)
+    torch.cuda.synchronize()
+    st = read_status(inp.q.device)
+    if st != 0:
+        raise SystemExit(json.dumps({"error": f"device status {st:#x} on the parity guard call"}))
+    sl = inp.seq_lens.tolist()
+    for b in range(inp.rows):
+        L = sl[b]
+        ids = out[b].long()
+        if L <= 2048:
+            continue
+        t = torch.arange(L, device=lg.device)
+        phys = inp.block_table[b, t // 64].long() * 64 + t % 64
+        inv = torch.full((int(phys.max()) + 1,), -1, dtype=torch.long, device=lg.device)
+        inv[phys] = t
+        ok = bool((ids >= 0).all()) and bool((ids <= phys.max()).all())
+        toks = inv[ids.clamp(0, int(phys.max()))]
+        ok = ok and bool((toks >= 0).all()) and int(torch.unique(toks).numel()) == 2048
+        if ok:
+            sel = torch.zeros(L, dtype=torch.bool, device=lg.device)
+            sel[toks] = True
+            row = lg[b, :L]
+            ok = bool(row[sel].min() >= row[~sel].max())
+        if not ok:
+            raise SystemExit(json.dumps({"error": f"parity guard failed on row {b}"}))
+
+
+def cpu_oracle_sample(inp_cpu: W.Inputs, budget_s: float):
+    """Times the CPU oracle (all host threads) on the first rows of the batch
+    (as many as fit in about budget_s).  Returns (GB/s, rows, seconds, threads)."""
+    from oracle import oracle  # CPU baseline leg only
+    d = inp_cpu.numpy()
+    threads = os.cpu_count() or 1
+
+    def run_rows(n):
+        t0 = time.perf_counter()
+        lg = oracle.logits(d["q"][:n], d["k_cache"], d["weights"][:n], d["seq_lens"][:n],
+                           d["block_table"][:n], num_pages=d["num_pages"], nthreads=threads)
+        oracle.topk(lg, d["seq_lens"][:n], d["block_table"][:n])
+        return time.perf_counter() - t0
+
+    t1 = run_rows(1)
+    n = int(max(1, min(inp_cpu.rows, budget_s / max(t1, 1e-3))))
+    dt = run_rows(n) if n > 1 else t1
+    sub = W.Inputs(inp_cpu.q[:n], inp_cpu.k_cache, inp_cpu.weights[:n], inp_cpu.seq_lens[:n],
+                   inp_cpu.block_table[:n])
+    return sub.algorithmic_bytes() / dt / 1e9, n, dt, threads
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    return world, rank, local
+
+
+def bench_ours(args, world, rank, local):
+    import torch.distributed as dist
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    seed = 100 * args.config + rank
+    base = W.config_inputs(args.config, seed=seed, device=dev)
+    sets = [base] + [W.Inputs(base.q.clone(), base.k_cache.clone(), base.weights.clone(), base.seq_lens.clone(),
+                              base.block_table.clone(), base.name, base.seed) for _ in range(N_SETS - 1)]
+    outs = [s.out() for s in sets]
+    parity_guard(base)
+    alg = base.algorithmic_bytes()
+    sbytes = score_bytes(base)
+    tokens = base.scored_tokens()
+
+    def step(i, ev=None):
+        s = sets[i % N_SETS]
+        run(s.q, s.k_cache, s.weights, s.seq_lens, s.block_table, outs[i % N_SETS], event_after_score=ev)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    n_ev = min(args.steps, 4096)
+    ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_m = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0.record()
+    for i in range(args.steps):
+        if i < n_ev:
+            ev_s[i].record()
+            step(i, ev_m[i])
+            ev_e[i].record()
+        else:
+            step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    elapsed = e0.elapsed_time(e1)  # ms
+    t = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_max = float(t.item())
+    score_ms = statistics.mean(ev_s[i].elapsed_time(ev_m[i]) for i in range(n_ev))
+    select_ms = statistics.mean(ev_m[i].elapsed_time(ev_e[i]) for i in range(n_ev))
+    ms_per_step = elapsed_max / args.steps
+    value = alg * world * args.steps / (elapsed_max / 1e3) / 1e9
+
+    # ---- end to end through the public entry point, host buffers
+    host = {k: getattr(base, k).cpu().pin_memory() for k in ("q", "k_cache", "weights", "seq_lens", "block_table")}
+    devb = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
+    out_h = torch.empty((base.rows, 2048), dtype=torch.int32).pin_memory()
+    out_d = base.out()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = out_h.numel() * 4
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+    def e2e_step():
+        for k, v in host.items():
+            devb[k].copy_(v, non_blocking=True)
+        kernel(devb["q"], devb["k_cache"], devb["weights"], devb["seq_lens"], devb["block_table"], out_d)
+        out_h.copy_(out_d, non_blocking=True)
+
+    for _ in range(min(3, args.warmup)):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    f1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / e2e_steps
+    e2e_value = alg * world / (e2e_ms / 1e3) / 1e9
+
+    if rank != 0:
+        return None
+    peak, peak_src = measured_hbm_peak()
+    achieved = sbytes / (score_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32 (scores), u32 keys (select)", "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": f"config{args.config}: {W.CONFIGS[args.config]}", "rows_per_gpu": base.rows,
+                   "scored_tokens_per_gpu": tokens, "pool_pages": base.num_pages, "max_pages": base.max_pages,
+                   "seed": seed, "l2": f"{N_SETS} rotating input copies of {base.k_cache.numel() / 1e6:.0f} MB K pool (> 126 MB L2)",
+                   "parallelism": f"rows sharded, dp{world}" if world > 1 else "single GPU"},
+        "tokens_per_s": round(tokens * world / (ms_per_step / 1e3), 1),
+        "frac_of_hbm_peak": round(value / world / peak, 4),
+        "frac_of_8tbs": round(value / world / 8000.0, 4),
+        "kernels_ms": {"score": round(score_ms, 5), "select": round(select_ms, 5)},
+        "roofline": {"kernel": "score_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "algorithmic_bytes_per_launch": sbytes, "traffic": None},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "kernel(...) drop-in, pinned host inputs"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        gbs, n, dt, threads = cpu_oracle_sample(base.to("cpu"), args.cpu_budget)
+        line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                                "sample": f"first {n} of {base.rows} rows of the same batch, full operator "
+                                          f"(exact C oracle: fp64 scores + top-2048), {dt:.2f} s"}
+    return line
+
+
+def bench_reference(args, world, rank):
+    """The CPU implementation of the path (the oracle port; the reference has
+    no CPU implementation of its own and its CUDA kernel is not installable
+    here), timed on the host cores."""
+    if rank != 0:
+        return None
+    from oracle import oracle
+    seed = 100 * args.config
+    inp = W.config_inputs(args.config, seed=seed, device="cpu")
+    d = inp.numpy()
+    threads = os.cpu_count() or 1
+
+    def one(n):
+        t0 = time.perf_counter()
+        lg = oracle.logits(d["q"][:n], d["k_cache"], d["weights"][:n], d["seq_lens"][:n], d["block_table"][:n],
+                           num_pages=d["num_pages"], nthreads=threads)
+        oracle.topk(lg, d["seq_lens"][:n], d["block_table"][:n])
+        return time.perf_counter() - t0
+
+    budget = args.ref_step_budget
+    t1 = one(1)
+    n = int(max(1, min(inp.rows, budget / max(t1, 1e-3))))
+    sub = W.Inputs(inp.q[:n], inp.k_cache, inp.weights[:n], inp.seq_lens[:n], inp.block_table[:n])
+    alg = sub.algorithmic_bytes()
+    for _ in range(args.warmup):
+        one(n)
+    times = [one(n) for _ in range(args.steps)]
+    step_s = statistics.mean(times)
+    value = alg / step_s / 1e9
+    sample = f"first {n} of {inp.rows} rows of config{args.config} per step (exact C oracle, fp64 scores + top-2048)"
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_s * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 scores, u32 keys",
+        "data": "synthetic (seeded)",
+        "config": {"workload": f"config{args.config}: {W.CONFIGS[args.config]}", "rows_sampled": n, "seed": seed},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")
+    ap.add_argument("--ref-step-budget", type=float, default=2.0, help="seconds per reference-arm step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    try:
+        line = bench_ours(args, world, rank, local) if args.impl == "ours" else bench_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1 and args.impl == "ours":
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

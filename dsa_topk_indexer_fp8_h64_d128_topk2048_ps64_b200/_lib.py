@@ -1,0 +1,138 @@
+"""ctypes binding of ``libdsai.so`` (the C ABI in ``include/dsai.h``).
+
+There is no fallback: if the library is missing or fails to load, importing
+the operator raises, and every call goes to the CUDA kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "libdsai.so"
+
+NUM_HEADS = 64
+HEAD_DIM = 128
+PAGE_SIZE = 64
+TOPK = 2048
+PAGE_BYTES = 8448
+SCALE_OFFSET = 8192
+
+DSAI_OK = 0
+STATUS_SEQLEN_CLAMPED = 0x1
+STATUS_BAD_PAGE = 0x2
+STATUS_WAIT_TIMEOUT = 0x4
+FLAG_SCORE_ALL_ROWS = 0x1
+
+EXPORTED_SYMBOLS = (
+    "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
+    "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
+)
+
+
+class DsaiArgs(ctypes.Structure):
+    """Mirror of ``dsai_args`` in include/dsai.h."""
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("k_cache", ctypes.c_void_p),
+        ("weights", ctypes.c_void_p),
+        ("seq_lens", ctypes.c_void_p),
+        ("block_table", ctypes.c_void_p),
+        ("topk_indices", ctypes.c_void_p),
+        ("logits_out", ctypes.c_void_p),
+        ("rows", ctypes.c_int32),
+        ("max_pages", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("ev_after_score", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: Path | None = None) -> ctypes.CDLL:
+    """Loads libdsai.so once; raises if it is missing."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        p = Path(path) if path else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"{p} is missing: build it with `python -m "
+                "dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200.build` (needs nvcc)")
+        lib = ctypes.CDLL(str(p))
+        vp, i32, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t
+        lib.dsai_workspace_size.argtypes = [i32, i32]
+        lib.dsai_workspace_size.restype = sz
+        lib.dsai_workspace_init.argtypes = [vp, sz, vp]
+        lib.dsai_workspace_init.restype = ctypes.c_int
+        lib.dsai_run.argtypes = [ctypes.POINTER(DsaiArgs), vp, sz, vp]
+        lib.dsai_run.restype = ctypes.c_int
+        lib.dsai_run_pairs.argtypes = [ctypes.POINTER(DsaiArgs), i32, vp, vp, vp, sz, vp]
+        lib.dsai_run_pairs.restype = ctypes.c_int
+        lib.dsai_merge_pairs.argtypes = [vp, vp, i32, vp, i32, vp, vp, vp]
+        lib.dsai_merge_pairs.restype = ctypes.c_int
+        lib.dsai_read_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
+        lib.dsai_read_status.restype = ctypes.c_int
+        lib.dsai_last_error.argtypes = []
+        lib.dsai_last_error.restype = ctypes.c_char_p
+        lib.dsai_version.argtypes = []
+        lib.dsai_version.restype = ctypes.c_char_p
+        _lib = lib
+        return lib
+
+
+def check(rc: int) -> None:
+    if rc != DSAI_OK:
+        msg = load_library().dsai_last_error().decode(errors="replace")
+        raise RuntimeError(f"dsai error {rc}: {msg}")
+
+
+def workspace_size(rows: int, max_pages: int) -> int:
+    return int(load_library().dsai_workspace_size(rows, max_pages))
+
+
+class Workspace:
+    """A device workspace for dsai_run, grown on demand (one per device and
+    stream user).  Its header holds the sticky device status word."""
+
+    def __init__(self, device: torch.device):
+        self.device = torch.device(device)
+        self.buf: torch.Tensor | None = None
+
+    def get(self, rows: int, max_pages: int, stream: int) -> tuple[int, int]:
+        need = workspace_size(rows, max_pages)
+        if self.buf is None or self.buf.numel() < need:
+            size = max(need, 1 << 20)
+            if self.buf is not None:
+                size = max(size, 2 * self.buf.numel())
+            self.buf = torch.empty(size, dtype=torch.uint8, device=self.device)
+            check(load_library().dsai_workspace_init(self.buf.data_ptr(), self.buf.numel(), stream))
+        return self.buf.data_ptr(), self.buf.numel()
+
+    def read_status(self, stream: int) -> int:
+        """Returns and clears the device status bits (synchronises `stream`)."""
+        if self.buf is None:
+            return 0
+        out = ctypes.c_int32(0)
+        check(load_library().dsai_read_status(self.buf.data_ptr(), stream, ctypes.byref(out)))
+        return int(out.value)
+
+
+_workspaces: dict[int, Workspace] = {}
+
+
+def default_workspace(device: torch.device) -> Workspace:
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None:
+        ws = _workspaces[idx] = Workspace(torch.device("cuda", idx))
+    return ws

@@ -1,0 +1,347 @@
+// api.cu — the C ABI (include/dsai.h): argument checks, TMA tensor maps,
+// workspace layout and the launch sequence.
+//
+// Replaces the reference's host dispatcher dsa_topk_indexer_cuda
+// (solution/python/kernel.cu:1208-1479).  Differences by design:
+//   * explicit caller-owned workspace instead of a static per-device scratch
+//     tensor (kernel.cu:1299-1323), so concurrent streams never share it;
+//   * error codes + dsai_last_error() instead of exceptions;
+//   * TMA tensor maps over the caller's buffers, encoded through the driver
+//     entry point (no link-time dependency on libcuda).
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DSAI_E_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  bool probed = false;
+  bool sm100 = false;
+  int sms = 0;
+};
+DeviceInfo g_dev[64];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(DSAI_E_UNSUPPORTED, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.probed) {
+    int major = 0, sms = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    d.sm100 = (major == 10);
+    d.sms = sms;
+    d.probed = true;
+  }
+  *out = d;
+  if (!d.sm100) return fail(DSAI_E_UNSUPPORTED, "device %d is not sm_100 (B200)", dev);
+  return DSAI_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor maps of one call.  Encoding is a host-only computation (~1 us); the
+// last few encodings are kept per thread, keyed by their arguments.
+struct MapKey {
+  const void* base;
+  uint64_t extent;
+  int kind;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && extent == o.extent && kind == o.kind;
+  }
+};
+struct MapEntry {
+  MapKey key{nullptr, 0, -1};
+  CUtensorMap map;
+};
+thread_local MapEntry g_maps[6];
+thread_local int g_maps_next = 0;
+
+enum MapKind { kMapQ = 0, kMapK = 1, kMapS = 2 };
+
+int get_map(int kind, const void* base, uint64_t extent, CUtensorMap* out) {
+  const MapKey key{base, extent, kind};
+  for (auto& e : g_maps)
+    if (e.key == key) {
+      *out = e.map;
+      return DSAI_OK;
+    }
+  auto enc = encode_fn();
+  if (!enc) return fail(DSAI_E_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  CUtensorMap m;
+  CUresult r;
+  if (kind == kMapQ) {  // q viewed as [rows*64, 128] bytes
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(dsai::kDim), extent};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(dsai::kDim)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(dsai::kDim), static_cast<cuuint32_t>(dsai::kHeads)};
+    cuuint32_t es[2] = {1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (kind == kMapK) {  // K values viewed as [num_pages, 64, 128] bytes, page stride 8448
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(dsai::kDim), static_cast<cuuint64_t>(dsai::kPage),
+                          extent};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(dsai::kDim),
+                             static_cast<cuuint64_t>(dsai::kPageBytes)};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(dsai::kDim), static_cast<cuuint32_t>(dsai::kPage), 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {  // scales viewed as [num_pages, 64] fp32 starting at byte 8192, page stride 8448
+    const void* sbase = static_cast<const uint8_t*>(base) + dsai::kScaleOff;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(dsai::kPage), extent};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(dsai::kPageBytes)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(dsai::kPage), 1};
+    cuuint32_t es[2] = {1, 1};
+    r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(sbase), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return fail(DSAI_E_CUDA, "cuTensorMapEncodeTiled(kind %d) failed: %d", kind, (int)r);
+  MapEntry& e = g_maps[g_maps_next];
+  g_maps_next = (g_maps_next + 1) % 6;
+  e.key = key;
+  e.map = m;
+  *out = m;
+  return DSAI_OK;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+size_t logits_bytes(int32_t rows, int32_t max_pages) {
+  const size_t b = static_cast<size_t>(rows) * static_cast<size_t>(max_pages) * dsai::kPage * sizeof(float);
+  return (b + 255) & ~static_cast<size_t>(255);
+}
+
+int check_args(const dsai_args* a, void* ws, size_t ws_bytes, bool need_ids) {
+  if (!a) return fail(DSAI_E_INVALID, "args is NULL");
+  if (a->rows < 0 || a->max_pages < 0 || a->num_pages < 0)
+    return fail(DSAI_E_INVALID, "negative size (rows=%d max_pages=%d num_pages=%d)", a->rows,
+                a->max_pages, a->num_pages);
+  if (a->rows == 0) return DSAI_OK;
+  if (!a->seq_lens || !a->block_table) return fail(DSAI_E_INVALID, "seq_lens / block_table is NULL");
+  if (need_ids && !a->topk_indices) return fail(DSAI_E_INVALID, "topk_indices is NULL");
+  if (!aligned(a->topk_indices, 16)) return fail(DSAI_E_INVALID, "topk_indices must be 16-B aligned");
+  if (!ws) return fail(DSAI_E_WORKSPACE, "workspace is NULL");
+  if (!aligned(ws, 256)) return fail(DSAI_E_WORKSPACE, "workspace must be 256-B aligned");
+  if (ws_bytes < dsai_workspace_size(a->rows, a->max_pages))
+    return fail(DSAI_E_WORKSPACE, "workspace too small: %zu < %zu", ws_bytes,
+                dsai_workspace_size(a->rows, a->max_pages));
+  return DSAI_OK;
+}
+
+int check_scoring_args(const dsai_args* a) {
+  if (!a->q || !a->k_cache || !a->weights) return fail(DSAI_E_INVALID, "q / k_cache / weights is NULL");
+  if (a->num_pages < 1) return fail(DSAI_E_INVALID, "num_pages must be >= 1");
+  if (!aligned(a->q, 16) || !aligned(a->k_cache, 16) || !aligned(a->weights, 16))
+    return fail(DSAI_E_INVALID, "q, k_cache and weights must be 16-B aligned");
+  if (a->logits_out && !aligned(a->logits_out, 16)) return fail(DSAI_E_INVALID, "logits_out must be 16-B aligned");
+  if (static_cast<long long>(a->max_pages) * dsai::kPage > (1ll << 30))
+    return fail(DSAI_E_INVALID, "max_pages too large");
+  return DSAI_OK;
+}
+
+// Scores all needed rows into `logits`, chunking by the per-launch row limit.
+int run_scoring(const dsai_args* a, float* logits, int* status, bool score_all, int sms,
+                cudaStream_t stream) {
+  CUtensorMap tq, tk, ts;
+  int rc = get_map(kMapQ, a->q, static_cast<uint64_t>(a->rows) * dsai::kHeads, &tq);
+  if (rc) return rc;
+  rc = get_map(kMapK, a->k_cache, static_cast<uint64_t>(a->num_pages), &tk);
+  if (rc) return rc;
+  rc = get_map(kMapS, a->k_cache, static_cast<uint64_t>(a->num_pages), &ts);
+  if (rc) return rc;
+  const int ld = a->max_pages * dsai::kPage;
+  for (int r0 = 0; r0 < a->rows; r0 += dsai::kMaxRowsPerLaunch) {
+    const int n = a->rows - r0 < dsai::kMaxRowsPerLaunch ? a->rows - r0 : dsai::kMaxRowsPerLaunch;
+    dsai::ScoreLaunch p;
+    p.weights = a->weights + static_cast<size_t>(r0) * dsai::kHeads;
+    p.seq_lens = a->seq_lens + r0;
+    p.block_table = a->block_table + static_cast<size_t>(r0) * a->max_pages;
+    p.logits = logits + static_cast<size_t>(r0) * ld;
+    p.status = status;
+    p.rows = n;
+    p.max_pages = a->max_pages;
+    p.num_pages = a->num_pages;
+    p.ld = ld;
+    p.row_base = r0;
+    p.score_all = score_all ? 1 : 0;
+    p.grid = sms;
+    cudaError_t e = dsai::launch_score(p, tq, tk, ts, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "score kernel launch");
+  }
+  return DSAI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t dsai_workspace_size(int32_t rows, int32_t max_pages) {
+  if (rows < 0 || max_pages < 0) return 0;
+  return dsai::kWsHeader + logits_bytes(rows, max_pages);
+}
+
+int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < dsai::kWsHeader) return fail(DSAI_E_WORKSPACE, "workspace too small");
+  cudaError_t e = cudaMemsetAsync(workspace, 0, dsai::kWsHeader, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace header)");
+  return DSAI_OK;
+}
+
+int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* stream_) {
+  int rc = check_args(a, workspace, workspace_bytes, true);
+  if (rc || a->rows == 0) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceInfo dev;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  int* status = static_cast<int*>(workspace);
+  const bool score_all = (a->flags & DSAI_FLAG_SCORE_ALL_ROWS) != 0;
+  const bool all_short = static_cast<long long>(a->max_pages) * dsai::kPage <= dsai::kTopK;
+
+  if (all_short && !score_all) {
+    // No row can exceed the top-K: the answer does not depend on scores.
+    if (a->ev_after_score) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    }
+    cudaError_t e = dsai::launch_short_rows(a->seq_lens, a->block_table, a->rows, a->max_pages,
+                                            a->topk_indices, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "short-rows kernel launch");
+    return DSAI_OK;
+  }
+  rc = check_scoring_args(a);
+  if (rc) return rc;
+  float* logits = a->logits_out ? a->logits_out
+                                : reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dsai::kWsHeader);
+  rc = run_scoring(a, logits, status, score_all, dev.sms, stream);
+  if (rc) return rc;
+  if (a->ev_after_score) {
+    cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  dsai::SelectLaunch sp;
+  sp.logits = logits;
+  sp.ld = a->max_pages * dsai::kPage;
+  sp.seq_lens = a->seq_lens;
+  sp.block_table = a->block_table;
+  sp.rows = a->rows;
+  sp.max_pages = a->max_pages;
+  sp.status = status;
+  sp.out_ids = a->topk_indices;
+  sp.out_scores = nullptr;
+  sp.out_tokens = nullptr;
+  sp.token_offset = 0;
+  cudaError_t e = dsai::launch_select(sp, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
+  return DSAI_OK;
+}
+
+int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, int32_t* out_tokens,
+                   void* workspace, size_t workspace_bytes, void* stream_) {
+  int rc = check_args(a, workspace, workspace_bytes, false);
+  if (rc || a->rows == 0) return rc;
+  if (!out_scores || !out_tokens) return fail(DSAI_E_INVALID, "out_scores / out_tokens is NULL");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  DeviceInfo dev;
+  rc = device_info(&dev);
+  if (rc) return rc;
+  rc = check_scoring_args(a);
+  if (rc) return rc;
+  int* status = static_cast<int*>(workspace);
+  float* logits = a->logits_out ? a->logits_out
+                                : reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dsai::kWsHeader);
+  rc = run_scoring(a, logits, status, true, dev.sms, stream);
+  if (rc) return rc;
+  if (a->ev_after_score) {
+    cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  dsai::SelectLaunch sp;
+  sp.logits = logits;
+  sp.ld = a->max_pages * dsai::kPage;
+  sp.seq_lens = a->seq_lens;
+  sp.block_table = a->block_table;
+  sp.rows = a->rows;
+  sp.max_pages = a->max_pages;
+  sp.status = status;
+  sp.out_ids = nullptr;
+  sp.out_scores = out_scores;
+  sp.out_tokens = out_tokens;
+  sp.token_offset = token_offset;
+  cudaError_t e = dsai::launch_select(sp, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
+  return DSAI_OK;
+}
+
+int dsai_merge_pairs(const float* scores, const int32_t* tokens, int32_t n_cand, const int32_t* bt_row,
+                     int32_t max_pages, const int32_t* seq_len, int32_t* out, void* stream_) {
+  if (n_cand < 0 || max_pages < 0) return fail(DSAI_E_INVALID, "negative size");
+  if (!bt_row || !seq_len || !out || (n_cand > 0 && (!scores || !tokens)))
+    return fail(DSAI_E_INVALID, "NULL pointer");
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  cudaError_t e = dsai::launch_merge(scores, tokens, n_cand, bt_row, max_pages, seq_len, out,
+                                     static_cast<cudaStream_t>(stream_));
+  if (e != cudaSuccess) return cuda_fail(e, "merge kernel launch");
+  return DSAI_OK;
+}
+
+int dsai_read_status(void* workspace, void* stream_, int32_t* status_out) {
+  if (!workspace || !status_out) return fail(DSAI_E_INVALID, "NULL pointer");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  int32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(workspace, 0, sizeof(int32_t), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "reading workspace status");
+  *status_out = v;
+  return DSAI_OK;
+}
+
+const char* dsai_last_error(void) { return g_err; }
+
+const char* dsai_version(void) { return "dsai 0.1.0 (sm_100a)"; }
+
+}  // extern "C"

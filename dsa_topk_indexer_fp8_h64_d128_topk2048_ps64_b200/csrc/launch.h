@@ -1,0 +1,58 @@
+// launch.h — internal launchers of the indexer kernels (host side).
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace dsai {
+
+struct ScoreLaunch {
+  const float* weights;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  float* logits;      // [rows, ld]
+  int* status;
+  int rows;
+  int max_pages;
+  int num_pages;
+  int ld;             // row stride of logits in floats (max_pages * 64)
+  int row_base;       // first row of this launch inside the q tensor map
+  int score_all;
+  int grid;
+};
+
+// Scores every scored row's tokens into `logits`.  The tensor maps describe
+// q ([rows*64, 128] u8, SW128), the K pages ([num_pages, 64, 128] u8, SW128)
+// and the per-token scales ([num_pages, 64] f32).
+cudaError_t launch_score(const ScoreLaunch& p, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
+                         const CUtensorMap& tmap_s, cudaStream_t stream);
+
+struct SelectLaunch {
+  const float* logits;  // [rows, ld]
+  int ld;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  int rows;
+  int max_pages;
+  int* status;
+  // Output: either physical ids, or (score, token + token_offset) pairs.
+  int32_t* out_ids;
+  float* out_scores;
+  int32_t* out_tokens;
+  int32_t token_offset;
+};
+
+cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream);
+
+cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,
+                              int max_pages, int32_t* out, cudaStream_t stream);
+
+cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
+                         const int32_t* bt_row, int max_pages, const int32_t* seq_len,
+                         int32_t* out, cudaStream_t stream);
+
+int score_smem_bytes();
+int select_smem_bytes();
+
+}  // namespace dsai

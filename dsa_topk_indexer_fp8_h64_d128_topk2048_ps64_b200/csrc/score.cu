@@ -1,0 +1,404 @@
+// score.cu — paged FP8 scoring of the index-K cache on tcgen05 tensor cores.
+//
+// For every scored row b and token t < L_b it writes the fp32 logit
+//   logit[b,t] = scale[page,slot] * sum_h ReLU(sum_d q[b,h,d] K[page,slot,d]) * w[b,h]
+// (the math of the reference's stage 1, solution/python/kernel.cu:5-9 and
+// :811-831, kept in fp32 instead of the reference's fp16 store).
+//
+// Work decomposition.  A row of L tokens is cut into ceil(L/128) tiles of two
+// 64-token pages (M = 128 of one UMMA).  All tiles of all scored rows form
+// one flat sequence; CTA c of a persistent grid takes the contiguous slice
+// [c*T/G, (c+1)*T/G), so every CTA moves the same number of K bytes and
+// crosses at most a few row boundaries (Q is reloaded only there).
+//
+// One CTA per SM, 6 warps, warp-specialised:
+//   warp 0      producer: follows block_table, TMA-loads each page (8 KB,
+//               128-B swizzle) and its 64 scales into an 8-stage ring, plus the
+//               row's Q (8 KB) into a 2-slot ring.  Block-table entries for 32
+//               tiles are fetched by the 32 lanes at once, so the pointer
+//               chase is off the issue path.
+//   warp 1      MMA issuer (one lane): 4 x tcgen05.mma kind::f8f6f4
+//               M128 N64 K32 per tile into one of 2 TMEM accumulators.
+//   warps 2-5   epilogue: tcgen05.ld of the 128x64 fp32 tile (one token per
+//               thread, 64 head scores in registers), ReLU, head weights,
+//               token scale, coalesced fp32 store.
+// Rows with L <= 2048 are skipped (their output does not depend on scores).
+#include "common.cuh"
+#include "launch.h"
+#include "sm100.cuh"
+
+namespace dsai {
+namespace {
+
+using namespace sm100;
+
+constexpr int kStages = 8;
+constexpr int kAccs = 2;
+constexpr int kAccCols = kHeads;               // 64 fp32 columns per accumulator
+constexpr int kTmemCols = kAccs * kAccCols;    // 128 (power of two >= 32)
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr uint32_t kPageTxBytes = kPageKBytes + kPage * 4;  // 8192 + 256
+
+struct ScoreParams {
+  const float* weights;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  float* logits;
+  int* status;
+  int rows;
+  int max_pages;
+  int num_pages;
+  int ld;
+  int row_base;
+  int score_all;
+};
+
+struct ScoreSmem {
+  uint8_t k[kStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
+  uint8_t q[2][kQBytes];                // SW128 K-major, N = 64 heads
+  float scale[kStages][kTileTok];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t qfull[2];
+  uint64_t qempty[2];
+  uint64_t tfull[kAccs];
+  uint64_t tempty[kAccs];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+  int warp_sums[kThreads / 32];
+  int row_start[kMaxRowsPerLaunch + 1];
+};
+
+constexpr int kSmemBytes = static_cast<int>(sizeof(ScoreSmem)) + 1024;
+
+// Last row r with row_start[r] <= t (t < row_start[rows]); that row is the
+// non-empty row holding tile t.
+__device__ __forceinline__ int find_row(const int* rs, int rows, int t) {
+  int lo = 0, hi = rows - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (rs[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Walks the tiles of a CTA's slice in order, tracking the row.
+struct Cursor {
+  int t, row, j, row_end;
+  __device__ void init(const int* rs, int rows, int t0) {
+    t = t0;
+    row = find_row(rs, rows, t0);
+    j = t0 - rs[row];
+    row_end = rs[row + 1];
+  }
+  __device__ void next(const int* rs, int t1) {
+    ++t;
+    ++j;
+    if (t < t1 && t == row_end) {
+      ++row;
+      while (rs[row + 1] <= t) ++row;
+      j = 0;
+      row_end = rs[row + 1];
+    }
+  }
+};
+
+__device__ __forceinline__ void fail(ScoreSmem& s, int* status) {
+  report(status, DSAI_STATUS_WAIT_TIMEOUT);
+  *reinterpret_cast<volatile int*>(&s.abort) = 1;
+}
+
+// Exclusive scan of per-row tile counts into s.row_start (all threads).
+__device__ void build_row_table(ScoreSmem& s, const ScoreParams& p) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (p.rows + kThreads - 1) / kThreads;
+  const int b0 = min(p.rows, tid * per), b1 = min(p.rows, b0 + per);
+  int* st = blockIdx.x == 0 ? p.status : nullptr;
+  int sum = 0;
+  for (int b = b0; b < b1; ++b)
+    sum += row_tiles(row_len(p.seq_lens, b, p.max_pages, st), p.score_all != 0);
+  int incl = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) s.warp_sums[warp] = incl;
+  __syncthreads();
+  int warp_excl = 0;
+  for (int w = 0; w < warp; ++w) warp_excl += s.warp_sums[w];
+  int prefix = warp_excl + incl - sum;
+  for (int b = b0; b < b1; ++b) {
+    s.row_start[b] = prefix;
+    prefix += row_tiles(row_len(p.seq_lens, b, p.max_pages, nullptr), p.score_all != 0);
+  }
+  if (tid == kThreads - 1) s.row_start[p.rows] = prefix;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    score_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                 const __grid_constant__ CUtensorMap tmap_k,
+                 const __grid_constant__ CUtensorMap tmap_s, const ScoreParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  ScoreSmem& s = *reinterpret_cast<ScoreSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  build_row_table(s, p);
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1 + kEpiThreads / 32);  // MMA commit + 4 epilogue warps
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.qfull[i], 1);
+      mbar_init(&s.qempty[i], 1);
+    }
+    for (int i = 0; i < kAccs; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], kEpiThreads / 32);
+    }
+    mbar_init(&s.drain, 1);
+    s.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmap_q);
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_s);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const int* rs = s.row_start;
+  const int T = rs[p.rows];
+  const int t0 = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / gridDim.x);
+  const int t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / gridDim.x);
+
+  if (t0 < t1) {
+    if (warp == 0) {
+      // ------------------------------------------------------------ producer
+      const uint64_t pol_k = l2_policy_evict_first();
+      const uint64_t pol_q = l2_policy_evict_last();
+      int stage = 0;
+      uint32_t phase = 0;
+      int qs = 1, cur_row = -1;
+      uint32_t qe_par[2] = {0u, 0u};
+      int q_uses[2] = {0, 0};
+      int fills[kStages];
+#pragma unroll
+      for (int i = 0; i < kStages; ++i) fills[i] = 0;
+      bool ok = true;
+      for (int tb = t0; tb < t1 && ok; tb += 32) {
+        // Lane i resolves tile tb+i: its row, pages and whether page 2 exists.
+        const int t = tb + lane;
+        int row = 0, pg0 = 0, pg1 = 0, two = 0;
+        if (t < t1) {
+          row = find_row(rs, p.rows, t);
+          const int j = t - rs[row];
+          const int L = row_len(p.seq_lens, row, p.max_pages, nullptr);
+          const int npages = (L + kPage - 1) / kPage;
+          const int32_t* bt = p.block_table + static_cast<size_t>(row) * p.max_pages;
+          two = (2 * j + 1) < npages;
+          pg0 = bt[2 * j];
+          pg1 = two ? bt[2 * j + 1] : 0;
+          if (static_cast<unsigned>(pg0) >= static_cast<unsigned>(p.num_pages) ||
+              static_cast<unsigned>(pg1) >= static_cast<unsigned>(p.num_pages))
+            report(p.status, DSAI_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range pages
+        }
+        const int n = min(32, t1 - tb);
+        for (int i = 0; i < n; ++i) {
+          const int r = __shfl_sync(0xffffffffu, row, i);
+          const int a = __shfl_sync(0xffffffffu, pg0, i);
+          const int b = __shfl_sync(0xffffffffu, pg1, i);
+          const int tw = __shfl_sync(0xffffffffu, two, i);
+          int good = 1;
+          if (lane == 0) {
+            if (r != cur_row) {
+              cur_row = r;
+              qs ^= 1;
+              if (!mbar_wait(&s.qempty[qs], qe_par[qs] ^ 1u, &s.abort, kWaitTimeoutNs)) {
+                good = 0;
+              } else {
+                qe_par[qs] ^= 1u;
+                ++q_uses[qs];
+                mbar_arrive_expect_tx(&s.qfull[qs], kQBytes);
+                tma_load_2d(s.q[qs], &tmap_q, &s.qfull[qs], 0, (p.row_base + r) * kHeads, pol_q);
+              }
+            }
+            if (good && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs))
+              good = 0;
+            if (good) {
+              mbar_arrive_expect_tx(&s.full[stage], tw ? 2 * kPageTxBytes : kPageTxBytes);
+              tma_load_3d(s.k[stage], &tmap_k, &s.full[stage], 0, 0, a, pol_k);
+              tma_load_2d(s.scale[stage], &tmap_s, &s.full[stage], 0, a, pol_k);
+              if (tw) {
+                tma_load_3d(s.k[stage] + kPageKBytes, &tmap_k, &s.full[stage], 0, 0, b, pol_k);
+                tma_load_2d(s.scale[stage] + kPage, &tmap_s, &s.full[stage], 0, b, pol_k);
+              }
+              ++fills[stage];
+              if (++stage == kStages) { stage = 0; phase ^= 1u; }
+            } else {
+              fail(s, p.status);
+            }
+          }
+          good = __shfl_sync(0xffffffffu, good, 0);
+          if (!good) { ok = false; break; }
+        }
+      }
+      // Never leave with a TMA in flight: wait for the latest fill of every
+      // stage and Q slot (all earlier fills were consumed, hence complete).
+      if (lane == 0) {
+        for (int i = 0; i < kStages; ++i)
+          if (fills[i] > 0 && !mbar_wait(&s.full[i], (fills[i] - 1) & 1, nullptr, kWaitTimeoutNs))
+            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+        for (int i = 0; i < 2; ++i)
+          if (q_uses[i] > 0 && !mbar_wait(&s.qfull[i], (q_uses[i] - 1) & 1, nullptr, kWaitTimeoutNs))
+            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc = make_idesc_e4m3_f32(kTileTok, kHeads);
+        int stage = 0, acc = 0, qs = 1, cur_row = -1;
+        uint32_t phase = 0, aphase = 0;
+        uint32_t qf_par[2] = {0u, 0u};
+        Cursor c;
+        c.init(rs, p.rows, t0);
+        for (; c.t < t1; c.next(rs, t1)) {
+          if (c.row != cur_row) {
+            if (cur_row >= 0) umma_commit(&s.qempty[qs]);  // previous row's Q free when done
+            cur_row = c.row;
+            qs ^= 1;
+            if (!mbar_wait(&s.qfull[qs], qf_par[qs], &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+            qf_par[qs] ^= 1u;
+          }
+          if (!mbar_wait(&s.full[stage], phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+          if (!mbar_wait(&s.tempty[acc], aphase ^ 1u, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.k[stage]));
+          const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.q[qs]));
+          const uint32_t d = s.tmem_base + static_cast<uint32_t>(acc * kAccCols);
+#pragma unroll
+          for (int kk = 0; kk < kDim / 32; ++kk)  // K = 32 e4m3 (32 B) per MMA
+            umma_f8(d, adesc + 2u * kk, bdesc + 2u * kk, idesc, kk > 0 ? 1u : 0u);
+          umma_commit(&s.empty[stage]);
+          umma_commit(&s.tfull[acc]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
+        }
+        // Every MMA issued by this thread has completed once this arrives.
+        umma_commit(&s.drain);
+        if (!mbar_wait(&s.drain, 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      }
+      __syncwarp();
+    } else {
+      // ------------------------------------------------------------ epilogue
+      const int quad = warp & 3;              // TMEM lanes [32*quad, 32*quad+32)
+      const int tok = quad * 32 + lane;       // token of the tile owned by this thread
+      int stage = 0, acc = 0, cur_row = -1, L = 0;
+      uint32_t phase = 0, aphase = 0;
+      float w[kHeads];
+      float* out_row = nullptr;
+      Cursor c;
+      c.init(rs, p.rows, t0);
+      for (; c.t < t1; c.next(rs, t1)) {
+        if (c.row != cur_row) {
+          cur_row = c.row;
+          const float4* w4 = reinterpret_cast<const float4*>(p.weights + static_cast<size_t>(cur_row) * kHeads);
+#pragma unroll
+          for (int i = 0; i < kHeads / 4; ++i) {
+            const float4 v = __ldg(w4 + i);
+            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+          }
+          L = row_len(p.seq_lens, cur_row, p.max_pages, nullptr);
+          out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
+        }
+        if (!mbar_wait(&s.full[stage], phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        if (!mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        const uint32_t taddr = s.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                               static_cast<uint32_t>(acc * kAccCols);
+        tmem_ld_32x32b_x32(taddr, r0);
+        tmem_ld_32x32b_x32(taddr + 32u, r1);
+        tmem_wait_ld();
+        tc_fence_before();
+        const float sc = s.scale[stage][tok];
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&s.tempty[acc]);
+          mbar_arrive(&s.empty[stage]);
+        }
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+        for (int h = 0; h < 32; h += 4) {
+          a0 = fmaf(fmaxf(__uint_as_float(r0[h + 0]), 0.f), w[h + 0], a0);
+          a1 = fmaf(fmaxf(__uint_as_float(r0[h + 1]), 0.f), w[h + 1], a1);
+          a2 = fmaf(fmaxf(__uint_as_float(r0[h + 2]), 0.f), w[h + 2], a2);
+          a3 = fmaf(fmaxf(__uint_as_float(r0[h + 3]), 0.f), w[h + 3], a3);
+        }
+#pragma unroll
+        for (int h = 0; h < 32; h += 4) {
+          a0 = fmaf(fmaxf(__uint_as_float(r1[h + 0]), 0.f), w[32 + h + 0], a0);
+          a1 = fmaf(fmaxf(__uint_as_float(r1[h + 1]), 0.f), w[32 + h + 1], a1);
+          a2 = fmaf(fmaxf(__uint_as_float(r1[h + 2]), 0.f), w[32 + h + 2], a2);
+          a3 = fmaf(fmaxf(__uint_as_float(r1[h + 3]), 0.f), w[32 + h + 3], a3);
+        }
+        const int t_abs = c.j * kTileTok + tok;
+        if (t_abs < L) out_row[t_abs] = ((a0 + a1) + (a2 + a3)) * sc;
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(s.tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace
+
+int score_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
+                         const CUtensorMap& tmap_s, cudaStream_t stream) {
+  static bool attr_set[64] = {};  // the attribute is per function and device
+  int dev = 0;
+  cudaError_t e0 = cudaGetDevice(&dev);
+  if (e0 != cudaSuccess) return e0;
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  ScoreParams p;
+  p.weights = lp.weights;
+  p.seq_lens = lp.seq_lens;
+  p.block_table = lp.block_table;
+  p.logits = lp.logits;
+  p.status = lp.status;
+  p.rows = lp.rows;
+  p.max_pages = lp.max_pages;
+  p.num_pages = lp.num_pages;
+  p.ld = lp.ld;
+  p.row_base = lp.row_base;
+  p.score_all = lp.score_all;
+  score_kernel<<<lp.grid, kThreads, kSmemBytes, stream>>>(tmap_q, tmap_k, tmap_s, p);
+  return cudaGetLastError();
+}
+
+}  // namespace dsai

@@ -1,0 +1,368 @@
+// select.cu — exact top-2048 selection over fp32 logits, and the merge of
+// partial (score, token) candidate lists.
+//
+// Keys are the order-preserving u32 image of the fp32 logit, so "top-K by
+// value" is "top-K by key".  Per row (one 1024-thread CTA):
+//   pass 1  histogram of the top 12 key bits (4096 bins) over all tokens,
+//           keys cached in shared memory when the row fits (<= 40960 tokens);
+//           the bin holding the K-th largest key is found by a block suffix
+//           scan;
+//   pass 2  tokens in higher bins are emitted directly; tokens in the pivot
+//           bin are compacted into a candidate list (<= 6144 entries, else
+//           the refinement below re-reads the row with a prefix filter);
+//   refine  10-bit + 10-bit histograms over the candidates give the exact
+//           32-bit pivot; candidates above it are emitted, and ties at the
+//           pivot fill the remaining slots in arbitrary order.
+// Histogram updates are warp-aggregated with __match_any_sync (lanes holding
+// the same bin add once), output slots are taken with one atomic per warp
+// via __ballot_sync.  The emitted set is exactly a top-K set of the logits;
+// among equal logits at the boundary the choice is arbitrary, as in the
+// reference's atomic emit (solution/python/kernel.cu:992-1018).
+//
+// Rows with seq_len <= 2048 emit ids of tokens 0..L-1 in token order and -1
+// padding (reference kernel.cu:897-905, :1079-1097).
+#include <cfloat>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace dsai {
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kBins1 = 4096;   // 12-bit first digit
+constexpr int kBins2 = 1024;   // 10-bit second and third digits
+constexpr int kCandCap = 6144;
+constexpr int kKeyCap = 40960;
+
+struct SelSmem {
+  uint32_t hist[kBins1];
+  uint32_t cand_key[kCandCap];
+  int32_t cand_idx[kCandCap];
+  uint32_t keys[kKeyCap];
+  int warp_tot[32];
+  int sel_bin;
+  int sel_above;
+  int out_count;
+  int cand_count;
+  int eq_count;
+};
+
+constexpr int kSmemBytes = static_cast<int>(sizeof(SelSmem));
+
+__device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool valid) {
+  const unsigned active = __ballot_sync(0xffffffffu, valid);
+  if (!valid) return;
+  const unsigned peers = __match_any_sync(active, bin);
+  if ((threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&hist[bin], __popc(peers));
+}
+
+// Warp-collective slot allocation: returns this lane's slot when pred holds.
+__device__ __forceinline__ int warp_alloc(int* counter, bool pred) {
+  const int lane = threadIdx.x & 31;
+  const unsigned m = __ballot_sync(0xffffffffu, pred);
+  int base = 0;
+  if (lane == 0 && m) base = atomicAdd(counter, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, 0);
+  return base + __popc(m & ((1u << lane) - 1u));
+}
+
+// Finds the bin holding the k-th largest entry: sel_bin = bin with
+// above(bin) < k <= above(bin) + hist[bin], sel_above = above(bin), where
+// above(bin) counts entries in higher bins.  nbins is 4096 or 1024.
+__device__ void find_threshold(SelSmem& s, int nbins, int k) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = nbins / kThreads;
+  const int lo = tid * per;
+  int sum = 0;
+  for (int i = 0; i < per; ++i) sum += s.hist[lo + i];
+  // inclusive suffix within the warp (higher lanes own higher bins)
+  int v = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_down_sync(0xffffffffu, v, off);
+    if (lane + off < 32) v += y;
+  }
+  if (lane == 0) s.warp_tot[warp] = v;
+  __syncthreads();
+  int warps_above = 0;
+  for (int w = warp + 1; w < kThreads / 32; ++w) warps_above += s.warp_tot[w];
+  int above = warps_above + (v - sum);
+  for (int i = per - 1; i >= 0; --i) {
+    const int h = s.hist[lo + i];
+    if (above < k && above + h >= k) {
+      s.sel_bin = lo + i;
+      s.sel_above = above;
+    }
+    above += h;
+  }
+  __syncthreads();
+}
+
+// Key source over one row of logits (key 0 never occurs for a finite or
+// infinite logit; it is used as "no entry").
+struct RowSrc {
+  const float* row;
+  __device__ __forceinline__ uint32_t key(int i) const { return ordered_key(row[i]); }
+};
+
+// Key source over a candidate list; padding (token -1) and tokens outside
+// the row [0, L) have key 0 and are never selected.
+struct CandSrc {
+  const float* scores;
+  const int32_t* tokens;
+  int L;
+  __device__ __forceinline__ uint32_t key(int i) const {
+    const int t = tokens[i];
+    return (t >= 0 && t < L) ? ordered_key(scores[i]) : 0u;
+  }
+};
+
+// Writes one selected entry: i is the source index, key its key.
+struct IdsOut {  // physical slot ids of tokens
+  int32_t* out;
+  const int32_t* bt_row;
+  __device__ __forceinline__ void emit(int pos, int i, uint32_t) const {
+    out[pos] = physical_id(bt_row, i);
+  }
+};
+struct PairsOut {  // (score, token + offset)
+  float* scores;
+  int32_t* tokens;
+  int32_t offset;
+  __device__ __forceinline__ void emit(int pos, int i, uint32_t key) const {
+    scores[pos] = key_to_float(key);
+    tokens[pos] = i + offset;
+  }
+};
+struct MergeOut {  // physical slot ids of candidate tokens
+  int32_t* out;
+  const int32_t* bt_row;
+  const int32_t* tokens;
+  __device__ __forceinline__ void emit(int pos, int i, uint32_t) const {
+    out[pos] = physical_id(bt_row, tokens[i]);
+  }
+};
+
+// Selects the kTopK largest keys among src[0, n) (at least kTopK valid).
+template <class Src, class Out>
+__device__ void select_topk(const Src& src, const Out& out, int n, SelSmem& s) {
+  const int tid = threadIdx.x;
+  const bool cached = n <= kKeyCap;
+
+  for (int i = tid; i < kBins1; i += kThreads) s.hist[i] = 0u;
+  if (tid == 0) {
+    s.out_count = 0;
+    s.cand_count = 0;
+    s.eq_count = 0;
+    s.sel_bin = 0;
+    s.sel_above = 0;
+  }
+  __syncthreads();
+
+  // pass 1: 12-bit histogram
+  for (int base = 0; base < n; base += kThreads) {
+    const int i = base + tid;
+    uint32_t key = 0u;
+    if (i < n) {
+      key = src.key(i);
+      if (cached) s.keys[i] = key;
+    }
+    hist_add(s.hist, key >> 20, key != 0u);
+  }
+  __syncthreads();
+  find_threshold(s, kBins1, kTopK);
+  const uint32_t bin1 = static_cast<uint32_t>(s.sel_bin);
+  const int k1 = kTopK - s.sel_above;
+  const int n1 = static_cast<int>(s.hist[bin1]);
+  const bool use_cand = n1 <= kCandCap;
+
+  // pass 2: emit above the pivot bin, compact the pivot bin
+  for (int base = 0; base < n; base += kThreads) {
+    const int i = base + tid;
+    uint32_t key = 0u;
+    if (i < n) key = cached ? s.keys[i] : src.key(i);
+    const uint32_t b = key >> 20;
+    const bool gt = key != 0u && b > bin1;
+    const bool eq = use_cand && key != 0u && b == bin1;
+    const int pos = warp_alloc(&s.out_count, gt);
+    if (gt) out.emit(pos, i, key);
+    const int cpos = warp_alloc(&s.cand_count, eq);
+    if (eq) {
+      s.cand_key[cpos] = key;
+      s.cand_idx[cpos] = i;
+    }
+  }
+  __syncthreads();
+
+  // Entries of the pivot bin: the candidate list, or the row re-read.
+  const int m = use_cand ? n1 : n;
+  auto bucket = [&](int j, uint32_t& key, int& idx) {
+    if (use_cand) {
+      key = s.cand_key[j];
+      idx = s.cand_idx[j];
+    } else {
+      key = cached ? s.keys[j] : src.key(j);
+      idx = j;
+      if (key == 0u || (key >> 20) != bin1) key = 0u;
+    }
+  };
+
+  // refine: bits [10, 20)
+  for (int i = tid; i < kBins2; i += kThreads) s.hist[i] = 0u;
+  __syncthreads();
+  for (int base = 0; base < m; base += kThreads) {
+    const int j = base + tid;
+    uint32_t key = 0u;
+    int idx = 0;
+    if (j < m) bucket(j, key, idx);
+    hist_add(s.hist, (key >> 10) & 1023u, key != 0u);
+  }
+  __syncthreads();
+  find_threshold(s, kBins2, k1);
+  const uint32_t bin2 = static_cast<uint32_t>(s.sel_bin);
+  const int k2 = k1 - s.sel_above;
+  const uint32_t prefix2 = (bin1 << 10) | bin2;
+
+  // refine: bits [0, 10)
+  for (int i = tid; i < kBins2; i += kThreads) s.hist[i] = 0u;
+  __syncthreads();
+  for (int base = 0; base < m; base += kThreads) {
+    const int j = base + tid;
+    uint32_t key = 0u;
+    int idx = 0;
+    if (j < m) bucket(j, key, idx);
+    hist_add(s.hist, key & 1023u, key != 0u && (key >> 10) == prefix2);
+  }
+  __syncthreads();
+  find_threshold(s, kBins2, k2);
+  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sel_bin);
+  const int k3 = k2 - s.sel_above;  // how many keys equal to the pivot are taken
+
+  for (int base = 0; base < m; base += kThreads) {
+    const int j = base + tid;
+    uint32_t key = 0u;
+    int idx = 0;
+    if (j < m) bucket(j, key, idx);
+    const bool gt = key != 0u && key > pivot;
+    const bool eq = key != 0u && key == pivot;
+    const int pos = warp_alloc(&s.out_count, gt);
+    if (gt) out.emit(pos, idx, key);
+    const int ticket = warp_alloc(&s.eq_count, eq);
+    if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, idx, key);
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelSmem& s = *reinterpret_cast<SelSmem*>(smem_raw);
+  const int b = blockIdx.x;
+  const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
+  const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
+  const float* row = p.logits + static_cast<size_t>(b) * p.ld;
+
+  if (p.out_ids) {
+    int32_t* out = p.out_ids + static_cast<size_t>(b) * kTopK;
+    if (L <= kTopK) {
+      for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
+      return;
+    }
+    select_topk(RowSrc{row}, IdsOut{out, bt_row}, L, s);
+  } else {
+    float* sc = p.out_scores + static_cast<size_t>(b) * kTopK;
+    int32_t* tk = p.out_tokens + static_cast<size_t>(b) * kTopK;
+    if (L <= kTopK) {
+      for (int i = threadIdx.x; i < kTopK; i += kThreads) {
+        sc[i] = i < L ? row[i] : -INFINITY;
+        tk[i] = i < L ? i + p.token_offset : -1;
+      }
+      return;
+    }
+    select_topk(RowSrc{row}, PairsOut{sc, tk, p.token_offset}, L, s);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    merge_kernel(const float* scores, const int32_t* tokens, int n_cand, const int32_t* bt_row,
+                 int max_pages, const int32_t* seq_len, int32_t* out) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SelSmem& s = *reinterpret_cast<SelSmem*>(smem_raw);
+  const int L = row_len(seq_len, 0, max_pages, nullptr);
+  if (L <= kTopK) {
+    for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
+    return;
+  }
+  // Slots stay -1 if the candidates hold fewer than kTopK real entries.
+  for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = -1;
+  __syncthreads();
+  select_topk(CandSrc{scores, tokens, L}, MergeOut{out, bt_row, tokens}, n_cand, s);
+}
+
+// Rows that all fit in the top-K (max_pages * 64 <= 2048): the output is the
+// physical ids of tokens 0..L-1 then -1, independent of q, K and weights
+// (reference fast path, solution/python/kernel.cu:1050-1099).  One 128-thread
+// CTA per row, 16-B stores.
+__global__ void __launch_bounds__(128) short_rows_kernel(const int32_t* seq_lens,
+                                                         const int32_t* block_table, int max_pages,
+                                                         int32_t* out) {
+  const int b = blockIdx.x;
+  const int L = row_len(seq_lens, b, max_pages, nullptr);
+  const int32_t* bt_row = block_table + static_cast<size_t>(b) * max_pages;
+  int4* out4 = reinterpret_cast<int4*>(out + static_cast<size_t>(b) * kTopK);
+  for (int v = threadIdx.x; v < kTopK / 4; v += 128) {
+    const int t = 4 * v;
+    int4 o;
+    o.x = t + 0 < L ? physical_id(bt_row, t + 0) : -1;
+    o.y = t + 1 < L ? physical_id(bt_row, t + 1) : -1;
+    o.z = t + 2 < L ? physical_id(bt_row, t + 2) : -1;
+    o.w = t + 3 < L ? physical_id(bt_row, t + 3) : -1;
+    out4[v] = o;
+  }
+}
+
+bool g_attr_done[64];
+
+cudaError_t ensure_attrs() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64 && g_attr_done[dev]) return cudaSuccess;
+  e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e != cudaSuccess) return e;
+  if (dev >= 0 && dev < 64) g_attr_done[dev] = true;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+int select_smem_bytes() { return kSmemBytes; }
+
+cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
+  cudaError_t e = ensure_attrs();
+  if (e != cudaSuccess) return e;
+  if (p.rows <= 0) return cudaSuccess;
+  select_kernel<<<p.rows, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,
+                              int max_pages, int32_t* out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  short_rows_kernel<<<rows, 128, 0, stream>>>(seq_lens, block_table, max_pages, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
+                         const int32_t* bt_row, int max_pages, const int32_t* seq_len,
+                         int32_t* out, cudaStream_t stream) {
+  cudaError_t e = ensure_attrs();
+  if (e != cudaSuccess) return e;
+  merge_kernel<<<1, kThreads, kSmemBytes, stream>>>(scores, tokens, n_cand, bt_row, max_pages,
+                                                    seq_len, out);
+  return cudaGetLastError();
+}
+
+}  // namespace dsai

@@ -1,0 +1,166 @@
+"""Drop-in entry point of the DSA top-K indexer.
+
+``kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table,
+topk_indices)`` has the signature, argument meaning and destination-passing
+style of the reference's ``solution/python/solution.py::kernel``
+(solution/python/solution.py:25-26, config.toml:6-9) and fails the same way:
+a ``RuntimeError`` for a tensor that is not CUDA / contiguous / of the
+expected dtype or shape (the reference's TORCH_CHECKs,
+solution/python/kernel.cu:1227-1240, :1273-1279).
+
+Everything runs in ``libdsai.so`` on the caller's current CUDA stream, with
+no host synchronisation.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+__all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status"]
+
+_FP8 = getattr(torch, "float8_e4m3fn", None)
+
+
+def _req(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_int32(t: torch.Tensor, name: str) -> None:
+    _req(t.is_cuda and t.is_contiguous() and t.dtype == torch.int32,
+         f"{name} must be int32 contiguous CUDA")
+
+
+def _check_scoring_inputs(q, k, w, rows: int) -> None:
+    _req(q.is_cuda and q.is_contiguous(), "q_index_fp8 must be contiguous CUDA")
+    _req(k.is_cuda and k.is_contiguous(), "k_index_cache_fp8 must be contiguous CUDA")
+    _req(w.is_cuda and w.is_contiguous() and w.dtype == torch.float32,
+         "weights must be float32 contiguous CUDA")
+    _req(q.dtype in (_FP8, torch.uint8, torch.int8), "q_index_fp8 must be float8_e4m3fn")
+    _req(q.numel() == rows * _lib.NUM_HEADS * _lib.HEAD_DIM, "q_index_fp8 shape must be [B, 64, 128]")
+    _req(k.element_size() == 1 and k.numel() % _lib.PAGE_BYTES == 0,
+         "k_index_cache_fp8 must be uint8 [num_pages, 64, 1, 132]")
+    _req(w.numel() == rows * _lib.NUM_HEADS, "weights shape must be [B, 64]")
+
+
+def _args(q, k, w, seq_lens, block_table, out, logits_out, flags: int) -> _lib.DsaiArgs:
+    rows, max_pages = int(block_table.size(0)), int(block_table.size(1))
+    a = _lib.DsaiArgs()
+    a.q = q.data_ptr() if q is not None else None
+    a.k_cache = k.data_ptr() if k is not None else None
+    a.weights = w.data_ptr() if w is not None else None
+    a.seq_lens = seq_lens.data_ptr()
+    a.block_table = block_table.data_ptr()
+    a.topk_indices = out.data_ptr() if out is not None else None
+    a.logits_out = logits_out.data_ptr() if logits_out is not None else None
+    a.rows = rows
+    a.max_pages = max_pages
+    a.num_pages = (k.numel() // _lib.PAGE_BYTES) if k is not None else 0
+    a.flags = flags
+    a.ev_after_score = None
+    return a
+
+
+def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices,
+        logits_out: torch.Tensor | None = None, score_all_rows: bool = False,
+        event_after_score: torch.cuda.Event | None = None, workspace: "_lib.Workspace | None" = None):
+    """The indexer with optional extras: ``logits_out`` ([B, max_pages*64]
+    fp32) receives the scored logits (entries at t >= seq_len are left
+    untouched; rows with seq_len <= 2048 are scored only with
+    ``score_all_rows``), ``event_after_score`` is recorded between the
+    scoring and the selection launches."""
+    _check_int32(block_table, "block_table")
+    _check_int32(seq_lens, "seq_lens")
+    _check_int32(topk_indices, "topk_indices")
+    rows, max_pages = int(block_table.size(0)), int(block_table.size(1))
+    _req(topk_indices.dim() == 2 and topk_indices.size(0) == rows and topk_indices.size(1) == _lib.TOPK,
+         "topk_indices shape must be [B, 2048]")
+    _req(seq_lens.numel() == rows, "seq_lens shape must be [B]")
+    if rows == 0:
+        return
+    lib = _lib.load_library()
+    needs_scoring = max_pages * _lib.PAGE_SIZE > _lib.TOPK or score_all_rows
+    if needs_scoring:
+        _check_scoring_inputs(q_index_fp8, k_index_cache_fp8, weights, rows)
+    if logits_out is not None:
+        _req(logits_out.is_cuda and logits_out.is_contiguous() and logits_out.dtype == torch.float32
+             and logits_out.numel() == rows * max_pages * _lib.PAGE_SIZE,
+             "logits_out must be float32 contiguous CUDA [B, max_pages*64]")
+    dev = block_table.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = workspace or _lib.default_workspace(dev)
+    ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
+    a = _args(q_index_fp8 if needs_scoring else None, k_index_cache_fp8 if needs_scoring else None,
+              weights if needs_scoring else None, seq_lens, block_table, topk_indices, logits_out,
+              _lib.FLAG_SCORE_ALL_ROWS if score_all_rows else 0)
+    if needs_scoring:
+        a.num_pages = k_index_cache_fp8.numel() // _lib.PAGE_BYTES
+    if event_after_score is not None:
+        a.ev_after_score = event_after_score.cuda_event
+    with torch.cuda.device(dev):
+        _lib.check(lib.dsai_run(ctypes.byref(a), ws_ptr, ws_bytes, stream))
+
+
+def kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):
+    """Drop-in for the reference's ``solution.py::kernel``: writes the top-2048
+    physical slot ids of every row into ``topk_indices`` ([B, 2048] int32,
+    -1 padded) and returns None."""
+    run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)
+
+
+def run_pairs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, token_offset: int,
+              out_scores: torch.Tensor, out_tokens: torch.Tensor,
+              workspace: "_lib.Workspace | None" = None):
+    """Per-row top-2048 (fp32 score, token + token_offset) pairs — the local
+    half of a page-range split of long rows across GPUs."""
+    _check_int32(block_table, "block_table")
+    _check_int32(seq_lens, "seq_lens")
+    rows, max_pages = int(block_table.size(0)), int(block_table.size(1))
+    _req(out_scores.is_cuda and out_scores.dtype == torch.float32 and out_scores.is_contiguous()
+         and out_scores.numel() == rows * _lib.TOPK, "out_scores must be float32 [B, 2048]")
+    _check_int32(out_tokens, "out_tokens")
+    _req(out_tokens.numel() == rows * _lib.TOPK, "out_tokens must be int32 [B, 2048]")
+    if rows == 0:
+        return
+    _check_scoring_inputs(q_index_fp8, k_index_cache_fp8, weights, rows)
+    lib = _lib.load_library()
+    dev = block_table.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = workspace or _lib.default_workspace(dev)
+    ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
+    a = _args(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, None, None, 0)
+    with torch.cuda.device(dev):
+        _lib.check(lib.dsai_run_pairs(ctypes.byref(a), int(token_offset), out_scores.data_ptr(),
+                                      out_tokens.data_ptr(), ws_ptr, ws_bytes, stream))
+
+
+def merge_pairs(scores: torch.Tensor, tokens: torch.Tensor, block_table_row: torch.Tensor,
+                seq_len: torch.Tensor, out: torch.Tensor):
+    """Top-2048 physical ids of ONE row from (score, token) candidates
+    gathered from several partial rows (token -1 = padding)."""
+    _req(scores.is_cuda and scores.dtype == torch.float32 and scores.is_contiguous(),
+         "scores must be float32 contiguous CUDA")
+    _check_int32(tokens, "tokens")
+    _check_int32(block_table_row, "block_table_row")
+    _check_int32(seq_len, "seq_len")
+    _check_int32(out, "out")
+    _req(scores.numel() == tokens.numel(), "scores and tokens must have the same length")
+    _req(out.numel() == _lib.TOPK, "out must hold 2048 int32")
+    lib = _lib.load_library()
+    dev = out.device
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        _lib.check(lib.dsai_merge_pairs(scores.data_ptr(), tokens.data_ptr(), int(scores.numel()),
+                                        block_table_row.data_ptr(), int(block_table_row.numel()),
+                                        seq_len.data_ptr(), out.data_ptr(), stream))
+
+
+def read_status(device=None) -> int:
+    """Returns and clears the device status bits of the default workspace of
+    `device` (synchronises its current stream)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = _lib.default_workspace(dev)
+    return ws.read_status(torch.cuda.current_stream(dev).cuda_stream)

@@ -1,0 +1,128 @@
+/*
+ * dsai.h — C ABI of the B200 (sm_100a) DSA lightning indexer.
+ *
+ * The operator: for every row b and token t in [0, seq_lens[b]) with
+ *   page = block_table[b, t/64], slot = t % 64,
+ *   S[h]       = sum_d q[b,h,d] * K[page,slot,d]          (e4m3 x e4m3, fp32 accumulate)
+ *   logit[b,t] = scale[page,slot] * sum_h ReLU(S[h]) * weights[b,h]
+ *   out[b,:]   = physical slot ids (page*64 + slot) of the 2048 largest logits,
+ *                rows with seq_len <= 2048 get ids of t = 0..seq_len-1 in
+ *                token order followed by -1 padding.
+ *
+ * Each entry point below replaces a piece of the reference's interface; the
+ * citation is given beside it (paths inside the reference project).
+ *
+ * Page layout in the index-K cache (k_cache, declared [num_pages,64,1,132] u8):
+ *   bytes [0, 8192)     64 tokens x 128 e4m3 values, token-major
+ *   bytes [8192, 8448)  64 little-endian fp32 scales
+ *
+ * All pointers are device pointers unless stated otherwise. Calls are
+ * asynchronous on `stream` and never synchronise the host; nothing is read
+ * back from the device.  Every function returns 0 (DSAI_OK) on success or a
+ * negative DSAI_E* code; dsai_last_error() gives the message of the last
+ * failure on the calling thread.
+ */
+#ifndef DSAI_H_
+#define DSAI_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define DSAI_API __attribute__((visibility("default")))
+#else
+#define DSAI_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSAI_NUM_HEADS 64
+#define DSAI_HEAD_DIM 128
+#define DSAI_PAGE_SIZE 64
+#define DSAI_TOPK 2048
+#define DSAI_PAGE_BYTES 8448
+#define DSAI_SCALE_OFFSET 8192
+
+/* Return codes. */
+#define DSAI_OK 0
+#define DSAI_E_INVALID (-1)   /* bad argument: null pointer, negative size, misalignment */
+#define DSAI_E_WORKSPACE (-2) /* workspace missing or smaller than dsai_workspace_size() */
+#define DSAI_E_CUDA (-3)      /* a CUDA runtime / driver call failed */
+#define DSAI_E_UNSUPPORTED (-4) /* device is not sm_100 or the library was built without it */
+
+/* Device status bits, accumulated in the workspace header by the kernels and
+ * read with dsai_read_status().  They never stop a call: the kernels clamp
+ * or zero-fill and carry on, so the output stays well defined. */
+#define DSAI_STATUS_SEQLEN_CLAMPED 0x1 /* a seq_len was < 0 or > max_pages*64 */
+#define DSAI_STATUS_BAD_PAGE 0x2       /* a block_table entry was outside [0, num_pages) */
+#define DSAI_STATUS_WAIT_TIMEOUT 0x4   /* a bounded on-chip wait gave up */
+
+/* Flags for dsai_args.flags. */
+#define DSAI_FLAG_SCORE_ALL_ROWS 0x1 /* also score rows with seq_len <= 2048 (debug logits) */
+
+typedef struct dsai_args {
+  const void* q;             /* [rows, 64, 128] float8_e4m3fn                         */
+  const void* k_cache;       /* [num_pages, 64, 1, 132] uint8, 8448 B per page         */
+  const float* weights;      /* [rows, 64] fp32                                        */
+  const int32_t* seq_lens;   /* [rows] int32                                           */
+  const int32_t* block_table;/* [rows, max_pages] int32                                */
+  int32_t* topk_indices;     /* [rows, 2048] int32, written                            */
+  float* logits_out;         /* optional [rows, max_pages*64] fp32; NULL = internal    */
+  int32_t rows;
+  int32_t max_pages;
+  int32_t num_pages;
+  int32_t flags;             /* DSAI_FLAG_*                                            */
+  void* ev_after_score;      /* optional cudaEvent_t recorded after the scoring launch */
+} dsai_args;
+
+/* Bytes of device workspace dsai_run needs for these sizes (256-B aligned
+ * base required).  Replaces the reference's per-device fp16 logits scratch
+ * (solution/python/kernel.cu:1299-1323). */
+DSAI_API size_t dsai_workspace_size(int32_t rows, int32_t max_pages);
+
+/* Zero the workspace header (status word).  Call once after allocating a
+ * workspace; the header is sticky between calls otherwise. */
+DSAI_API int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* The indexer, destination-passing.  Replaces the reference's extension op
+ * `run` / dsa_topk_indexer_cuda (solution/python/kernel.cu:1208-1479) that
+ * solution.py::kernel (solution/python/solution.py:25-26) forwards to, and the
+ * TVM-FFI export `kernel` (solution/cuda/kernel.cu:430-507). */
+DSAI_API int dsai_run(const dsai_args* args, void* workspace, size_t workspace_bytes,
+             void* stream);
+
+/* Per-row top-2048 as (fp32 score, token index + token_offset) pairs, for a
+ * caller that merges several partial rows (a long row split by page range
+ * across GPUs).  Rows with seq_len <= 2048 give all their tokens, padded with
+ * (-inf, -1).  No reference counterpart: the reference is single-GPU; this
+ * is the local half of the page-range split. */
+DSAI_API int dsai_run_pairs(const dsai_args* args, int32_t token_offset,
+                   float* out_scores, int32_t* out_tokens, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Merge n_cand (score, token) candidates of ONE row into its top-2048
+ * physical slot ids, using that row's full block table (bt_row, max_pages
+ * entries) and its seq_len.  Token -1 marks padding.  When the row has
+ * seq_len <= 2048 the output is token order then -1, as dsai_run gives.
+ * No reference counterpart (the merge half of the page-range split). */
+DSAI_API int dsai_merge_pairs(const float* scores, const int32_t* tokens, int32_t n_cand,
+                     const int32_t* bt_row, int32_t max_pages,
+                     const int32_t* seq_len, int32_t* out, void* stream);
+
+/* Copy the workspace status word to *status_out (host), then clear it.
+ * Synchronises `stream`. */
+DSAI_API int dsai_read_status(void* workspace, void* stream, int32_t* status_out);
+
+/* Message of the last failure on this thread ("" if none). */
+DSAI_API const char* dsai_last_error(void);
+
+/* Library version string. */
+DSAI_API const char* dsai_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSAI_H_ */

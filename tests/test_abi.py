@@ -1,0 +1,92 @@
+"""CPU tests of the C ABI: the library loads without a GPU, exports every
+function include/dsai.h declares, sizes its workspace, and rejects bad
+arguments before touching the device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "dsai.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    return re.findall(r"DSAI_API\s+[\w\s\*]+?\b(dsai_\w+)\s*\(", text)
+
+
+def test_header_declares_the_api():
+    names = declared_functions()
+    assert set(names) == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(dsai_lib):
+    for name in declared_functions():
+        assert hasattr(dsai_lib, name), name
+    assert dsai_lib.dsai_version().decode().startswith("dsai")
+
+
+def test_only_the_api_is_exported(dsai_lib):
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("nm unavailable")
+    exported = {l.split()[-1] for l in out.stdout.splitlines() if " T " in l}
+    dsai = {s for s in exported if s.startswith("dsai_")}
+    assert dsai == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_workspace_size(dsai_lib):
+    assert dsai_lib.dsai_workspace_size(0, 0) == 256
+    assert dsai_lib.dsai_workspace_size(64, 512) == 256 + 64 * 512 * 64 * 4
+    assert dsai_lib.dsai_workspace_size(3, 5) == 256 + ((3 * 5 * 64 * 4 + 255) // 256) * 256
+    assert dsai_lib.dsai_workspace_size(-1, 4) == 0
+
+
+def _args(**kw):
+    a = _lib.DsaiArgs()
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_run_rejects_bad_arguments_without_device(dsai_lib):
+    assert dsai_lib.dsai_run(None, None, 0, None) == -1
+    assert b"NULL" in dsai_lib.dsai_last_error()
+    a = _args(rows=-2, max_pages=4, num_pages=4)
+    assert dsai_lib.dsai_run(ctypes.byref(a), None, 0, None) == -1
+    assert b"negative" in dsai_lib.dsai_last_error()
+    # zero rows is a no-op success
+    a = _args(rows=0, max_pages=4, num_pages=4)
+    assert dsai_lib.dsai_run(ctypes.byref(a), None, 0, None) == 0
+    # missing workspace / too small / misaligned
+    a = _args(rows=2, max_pages=4, num_pages=4, seq_lens=16, block_table=32, topk_indices=64)
+    assert dsai_lib.dsai_run(ctypes.byref(a), None, 0, None) == -2
+    assert dsai_lib.dsai_run(ctypes.byref(a), 256, 16, None) == -2
+    assert b"too small" in dsai_lib.dsai_last_error()
+    assert dsai_lib.dsai_run(ctypes.byref(a), 300, 1 << 20, None) == -2
+    assert b"aligned" in dsai_lib.dsai_last_error()
+    a = _args(rows=2, max_pages=4, num_pages=4, seq_lens=16, block_table=32, topk_indices=68)
+    assert dsai_lib.dsai_run(ctypes.byref(a), 256, 1 << 20, None) == -1
+    a = _args(rows=2, max_pages=4, num_pages=4, seq_lens=None, block_table=32, topk_indices=64)
+    assert dsai_lib.dsai_run(ctypes.byref(a), 256, 1 << 20, None) == -1
+
+
+def test_merge_and_status_reject_null(dsai_lib):
+    assert dsai_lib.dsai_merge_pairs(None, None, -1, None, 4, None, None, None) == -1
+    assert dsai_lib.dsai_merge_pairs(None, None, 4, 16, 4, 16, 16, None) == -1
+    assert dsai_lib.dsai_read_status(None, None, None) == -1
+
+
+def test_python_entry_validates_like_the_reference():
+    """The drop-in raises RuntimeError for non-CUDA / wrong-dtype tensors, as
+    the reference's TORCH_CHECKs do."""
+    import torch
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import kernel
+    bt = torch.zeros((2, 4), dtype=torch.int32)
+    sl = torch.zeros(2, dtype=torch.int32)
+    out = torch.zeros((2, 2048), dtype=torch.int32)
+    with pytest.raises(RuntimeError, match="block_table must be int32 contiguous CUDA"):
+        kernel(None, None, None, sl, bt, out)

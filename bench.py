@@ -217,6 +217,10 @@ def bench_ours(args, world, rank, local):
     ev_s = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     ev_m = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     ev_e = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    # ev_m is recorded inside the library (between its two launches); torch only
+    # allows elapsed_time on events it has seen recorded, so record them once here.
+    for ev in ev_m:
+        ev.record()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(dev)
     if world > 1:

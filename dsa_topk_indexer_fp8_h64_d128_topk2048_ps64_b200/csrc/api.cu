@@ -13,7 +13,9 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <climits>
 #include <mutex>
+#include <unordered_map>
 
 #include "common.cuh"
 #include "launch.h"
@@ -145,11 +147,50 @@ int get_map(int kind, const void* base, uint64_t extent, CUtensorMap* out) {
   return DSAI_OK;
 }
 
+// Histogram rows known to be zero, per workspace.  Every call leaves the
+// histograms of its `rows` rows zero, but its logits start right after them,
+// so a later call with more rows finds the extra histogram rows dirty; those
+// (and only those) are cleared before scoring.  dsai_workspace_init marks a
+// whole workspace clean.
+std::mutex g_ws_mu;
+std::unordered_map<const void*, int32_t> g_ws_clean_rows;
+
+int prepare_hist(void* ws, int32_t rows, cudaStream_t stream) {
+  int32_t clean = 0;
+  {
+    std::lock_guard<std::mutex> g(g_ws_mu);
+    auto it = g_ws_clean_rows.find(ws);
+    if (it != g_ws_clean_rows.end()) clean = it->second;
+    g_ws_clean_rows[ws] = rows;
+  }
+  if (rows > clean) {
+    uint8_t* base = static_cast<uint8_t*>(ws) + dsai::kWsHeader +
+                    static_cast<size_t>(clean) * dsai::kHistBins * sizeof(uint32_t);
+    const size_t bytes = static_cast<size_t>(rows - clean) * dsai::kHistBins * sizeof(uint32_t);
+    cudaError_t e = cudaMemsetAsync(base, 0, bytes, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(histograms)");
+  }
+  return DSAI_OK;
+}
+
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Workspace layout: [header 256 B | per-row first-digit histograms | logits].
+size_t hist_bytes(int32_t rows) {
+  return static_cast<size_t>(rows) * dsai::kHistBins * sizeof(uint32_t);
+}
 
 size_t logits_bytes(int32_t rows, int32_t max_pages) {
   const size_t b = static_cast<size_t>(rows) * static_cast<size_t>(max_pages) * dsai::kPage * sizeof(float);
   return (b + 255) & ~static_cast<size_t>(255);
+}
+
+uint32_t* ws_hist(void* ws) {
+  return reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader);
+}
+
+float* ws_logits(void* ws, int32_t rows) {
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader + hist_bytes(rows));
 }
 
 int check_args(const dsai_args* a, void* ws, size_t ws_bytes, bool need_ids) {
@@ -181,7 +222,7 @@ int check_scoring_args(const dsai_args* a) {
 }
 
 // Scores all needed rows into `logits`, chunking by the per-launch row limit.
-int run_scoring(const dsai_args* a, float* logits, int* status, bool score_all, int sms,
+int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, bool score_all, int sms,
                 cudaStream_t stream) {
   CUtensorMap tq, tk, ts;
   int rc = get_map(kMapQ, a->q, static_cast<uint64_t>(a->rows) * dsai::kHeads, &tq);
@@ -198,6 +239,7 @@ int run_scoring(const dsai_args* a, float* logits, int* status, bool score_all, 
     p.seq_lens = a->seq_lens + r0;
     p.block_table = a->block_table + static_cast<size_t>(r0) * a->max_pages;
     p.logits = logits + static_cast<size_t>(r0) * ld;
+    p.hist = hist + static_cast<size_t>(r0) * dsai::kHistBins;
     p.status = status;
     p.rows = n;
     p.max_pages = a->max_pages;
@@ -218,13 +260,15 @@ extern "C" {
 
 size_t dsai_workspace_size(int32_t rows, int32_t max_pages) {
   if (rows < 0 || max_pages < 0) return 0;
-  return dsai::kWsHeader + logits_bytes(rows, max_pages);
+  return dsai::kWsHeader + hist_bytes(rows) + logits_bytes(rows, max_pages);
 }
 
 int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace || workspace_bytes < dsai::kWsHeader) return fail(DSAI_E_WORKSPACE, "workspace too small");
-  cudaError_t e = cudaMemsetAsync(workspace, 0, dsai::kWsHeader, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace header)");
+  cudaError_t e = cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
+  std::lock_guard<std::mutex> g(g_ws_mu);
+  g_ws_clean_rows[workspace] = INT_MAX;
   return DSAI_OK;
 }
 
@@ -252,9 +296,11 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   }
   rc = check_scoring_args(a);
   if (rc) return rc;
-  float* logits = a->logits_out ? a->logits_out
-                                : reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dsai::kWsHeader);
-  rc = run_scoring(a, logits, status, score_all, dev.sms, stream);
+  float* logits = a->logits_out ? a->logits_out : ws_logits(workspace, a->rows);
+  uint32_t* hist = ws_hist(workspace);
+  rc = prepare_hist(workspace, a->rows, stream);
+  if (rc) return rc;
+  rc = run_scoring(a, logits, hist, status, score_all, dev.sms, stream);
   if (rc) return rc;
   if (a->ev_after_score) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
@@ -263,6 +309,7 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   dsai::SelectLaunch sp;
   sp.logits = logits;
   sp.ld = a->max_pages * dsai::kPage;
+  sp.hist = hist;
   sp.seq_lens = a->seq_lens;
   sp.block_table = a->block_table;
   sp.rows = a->rows;
@@ -289,9 +336,11 @@ int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, 
   rc = check_scoring_args(a);
   if (rc) return rc;
   int* status = static_cast<int*>(workspace);
-  float* logits = a->logits_out ? a->logits_out
-                                : reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dsai::kWsHeader);
-  rc = run_scoring(a, logits, status, true, dev.sms, stream);
+  float* logits = a->logits_out ? a->logits_out : ws_logits(workspace, a->rows);
+  uint32_t* hist = ws_hist(workspace);
+  rc = prepare_hist(workspace, a->rows, stream);
+  if (rc) return rc;
+  rc = run_scoring(a, logits, hist, status, true, dev.sms, stream);
   if (rc) return rc;
   if (a->ev_after_score) {
     cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
@@ -300,6 +349,7 @@ int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, 
   dsai::SelectLaunch sp;
   sp.logits = logits;
   sp.ld = a->max_pages * dsai::kPage;
+  sp.hist = hist;
   sp.seq_lens = a->seq_lens;
   sp.block_table = a->block_table;
   sp.rows = a->rows;

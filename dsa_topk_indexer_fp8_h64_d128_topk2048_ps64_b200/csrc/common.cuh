@@ -27,6 +27,13 @@ constexpr int kQBytes = kHeads * kDim;        // 8192 B of Q per row
 // the host splits larger batches into several launches.
 constexpr int kMaxRowsPerLaunch = 4096;
 
+// First radix digit of the selection: the top 12 bits of the ordered key
+// (sign, 8 exponent bits, 3 mantissa bits).  The scorer builds a per-row
+// histogram of it in the workspace; the selection kernel consumes it and
+// clears it again for the next call.
+constexpr int kHistBits = 12;
+constexpr int kHistBins = 1 << kHistBits;
+
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s bound on any on-chip wait
 
 // Workspace header: status word at offset 0, data from kWsHeader on.

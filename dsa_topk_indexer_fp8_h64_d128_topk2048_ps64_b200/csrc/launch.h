@@ -12,6 +12,7 @@ struct ScoreLaunch {
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* logits;      // [rows, ld]
+  uint32_t* hist;     // [rows, kHistBins] first-digit histograms (zero on entry)
   int* status;
   int rows;
   int max_pages;
@@ -31,6 +32,7 @@ cudaError_t launch_score(const ScoreLaunch& p, const CUtensorMap& tmap_q, const 
 struct SelectLaunch {
   const float* logits;  // [rows, ld]
   int ld;
+  uint32_t* hist;       // [rows, kHistBins] from the scoring launch; cleared here
   const int32_t* seq_lens;
   const int32_t* block_table;
   int rows;

@@ -3,7 +3,9 @@
 // For every scored row b and token t < L_b it writes the fp32 logit
 //   logit[b,t] = scale[page,slot] * sum_h ReLU(sum_d q[b,h,d] K[page,slot,d]) * w[b,h]
 // (the math of the reference's stage 1, solution/python/kernel.cu:5-9 and
-// :811-831, kept in fp32 instead of the reference's fp16 store).
+// :811-831, kept in fp32 instead of the reference's fp16 store), and the
+// per-row histogram of the logits' top 12 ordered-key bits that the
+// selection kernel starts from.
 //
 // Work decomposition.  A row of L tokens is cut into ceil(L/128) tiles of two
 // 64-token pages (M = 128 of one UMMA).  All tiles of all scored rows form
@@ -12,16 +14,20 @@
 // crosses at most a few row boundaries (Q is reloaded only there).
 //
 // One CTA per SM, 6 warps, warp-specialised:
-//   warp 0      producer: follows block_table, TMA-loads each page (8 KB,
-//               128-B swizzle) and its 64 scales into an 8-stage ring, plus the
-//               row's Q (8 KB) into a 2-slot ring.  Block-table entries for 32
-//               tiles are fetched by the 32 lanes at once, so the pointer
-//               chase is off the issue path.
+//   warp 0      producer: follows block_table and TMA-loads each page (8 KB,
+//               128-B swizzle) into a 10-stage K ring, its 64 scales into a
+//               16-slot scale ring, and the row's Q (8 KB) into a 2-slot ring.
+//               The 32 lanes resolve the pages of 32 tiles at once, one batch
+//               ahead, so the block-table pointer chase never stalls issue.
 //   warp 1      MMA issuer (one lane): 4 x tcgen05.mma kind::f8f6f4
-//               M128 N64 K32 per tile into one of 2 TMEM accumulators.
+//               M128 N64 K32 per tile into one of 4 TMEM accumulators.  A K
+//               stage is released as soon as its MMAs complete.
 //   warps 2-5   epilogue: tcgen05.ld of the 128x64 fp32 tile (one token per
 //               thread, 64 head scores in registers), ReLU, head weights,
-//               token scale, coalesced fp32 store.
+//               token scale, coalesced fp32 store, and one fire-and-forget
+//               reduction into the row's global histogram of 12-bit key
+//               prefixes (no group synchronisation, so a timed-out warp can
+//               never leave the others waiting).
 // Rows with L <= 2048 are skipped (their output does not depend on scores).
 #include "common.cuh"
 #include "launch.h"
@@ -32,19 +38,21 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 8;
-constexpr int kAccs = 2;
+constexpr int kStages = 10;
+constexpr int kScaleSlots = 16;
+constexpr int kAccs = 4;
 constexpr int kAccCols = kHeads;               // 64 fp32 columns per accumulator
-constexpr int kTmemCols = kAccs * kAccCols;    // 128 (power of two >= 32)
+constexpr int kTmemCols = kAccs * kAccCols;    // 256 (power of two >= 32)
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
-constexpr uint32_t kPageTxBytes = kPageKBytes + kPage * 4;  // 8192 + 256
+constexpr uint32_t kScaleTx = kPage * 4;       // 256 B of scales per page
 
 struct ScoreParams {
   const float* weights;
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* logits;
+  uint32_t* hist;     // [rows, kHistBins] (rows of this launch)
   int* status;
   int rows;
   int max_pages;
@@ -57,9 +65,11 @@ struct ScoreParams {
 struct ScoreSmem {
   uint8_t k[kStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
   uint8_t q[2][kQBytes];                // SW128 K-major, N = 64 heads
-  float scale[kStages][kTileTok];
+  float scale[kScaleSlots][kTileTok];
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  uint64_t sfull[kScaleSlots];
+  uint64_t sempty[kScaleSlots];
   uint64_t qfull[2];
   uint64_t qempty[2];
   uint64_t tfull[kAccs];
@@ -72,6 +82,7 @@ struct ScoreSmem {
 };
 
 constexpr int kSmemBytes = static_cast<int>(sizeof(ScoreSmem)) + 1024;
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Last row r with row_start[r] <= t (t < row_start[rows]); that row is the
 // non-empty row holding tile t.
@@ -137,6 +148,25 @@ __device__ void build_row_table(ScoreSmem& s, const ScoreParams& p) {
   if (tid == kThreads - 1) s.row_start[p.rows] = prefix;
 }
 
+// Page ids of one tile, resolved by one producer lane.
+struct TileRef {
+  int row, pg0, pg1, two;
+};
+
+__device__ __forceinline__ TileRef resolve_tile(const ScoreSmem& s, const ScoreParams& p, int t) {
+  TileRef r;
+  r.row = find_row(s.row_start, p.rows, t);
+  const int j = t - s.row_start[r.row];
+  const int32_t* bt = p.block_table + static_cast<size_t>(r.row) * p.max_pages;
+  // The second page is read unconditionally when it is inside the row of the
+  // block table (in bounds); it is used only when the row reaches it.
+  const int L = row_len(p.seq_lens, r.row, p.max_pages, nullptr);
+  r.pg0 = bt[2 * j];
+  r.pg1 = (2 * j + 1 < p.max_pages) ? bt[2 * j + 1] : 0;
+  r.two = (2 * j + 1) * kPage < L;
+  return r;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     score_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  const __grid_constant__ CUtensorMap tmap_k,
@@ -150,7 +180,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1 + kEpiThreads / 32);  // MMA commit + 4 epilogue warps
+      mbar_init(&s.empty[i], 1);                 // MMA commit
+    }
+    for (int i = 0; i < kScaleSlots; ++i) {
+      mbar_init(&s.sfull[i], 1);
+      mbar_init(&s.sempty[i], kEpiThreads / 32);  // 4 epilogue warps
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.qfull[i], 1);
@@ -187,38 +221,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------------------ producer
       const uint64_t pol_k = l2_policy_evict_first();
       const uint64_t pol_q = l2_policy_evict_last();
-      int stage = 0;
-      uint32_t phase = 0;
-      int qs = 1, cur_row = -1;
+      int stage = 0, sslot = 0, qs = 1, cur_row = -1;
+      uint32_t phase = 0, sphase = 0;
       uint32_t qe_par[2] = {0u, 0u};
       int q_uses[2] = {0, 0};
-      int fills[kStages];
-#pragma unroll
-      for (int i = 0; i < kStages; ++i) fills[i] = 0;
+      int k_fills = 0, s_fills = 0;
       bool ok = true;
+      TileRef nxt = {0, 0, 0, 0};
+      if (t0 + lane < t1) nxt = resolve_tile(s, p, t0 + lane);
       for (int tb = t0; tb < t1 && ok; tb += 32) {
-        // Lane i resolves tile tb+i: its row, pages and whether page 2 exists.
-        const int t = tb + lane;
-        int row = 0, pg0 = 0, pg1 = 0, two = 0;
-        if (t < t1) {
-          row = find_row(rs, p.rows, t);
-          const int j = t - rs[row];
-          const int L = row_len(p.seq_lens, row, p.max_pages, nullptr);
-          const int npages = (L + kPage - 1) / kPage;
-          const int32_t* bt = p.block_table + static_cast<size_t>(row) * p.max_pages;
-          two = (2 * j + 1) < npages;
-          pg0 = bt[2 * j];
-          pg1 = two ? bt[2 * j + 1] : 0;
-          if (static_cast<unsigned>(pg0) >= static_cast<unsigned>(p.num_pages) ||
-              static_cast<unsigned>(pg1) >= static_cast<unsigned>(p.num_pages))
-            report(p.status, DSAI_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range pages
-        }
+        const TileRef cur = nxt;
+        // Resolve the next batch now; its loads overlap this batch's issue.
+        if (tb + 32 + lane < t1) nxt = resolve_tile(s, p, tb + 32 + lane);
+        if (tb + lane < t1 &&
+            (static_cast<unsigned>(cur.pg0) >= static_cast<unsigned>(p.num_pages) ||
+             (cur.two && static_cast<unsigned>(cur.pg1) >= static_cast<unsigned>(p.num_pages))))
+          report(p.status, DSAI_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range pages
         const int n = min(32, t1 - tb);
         for (int i = 0; i < n; ++i) {
-          const int r = __shfl_sync(0xffffffffu, row, i);
-          const int a = __shfl_sync(0xffffffffu, pg0, i);
-          const int b = __shfl_sync(0xffffffffu, pg1, i);
-          const int tw = __shfl_sync(0xffffffffu, two, i);
+          const int r = __shfl_sync(0xffffffffu, cur.row, i);
+          const int a = __shfl_sync(0xffffffffu, cur.pg0, i);
+          const int b = __shfl_sync(0xffffffffu, cur.pg1, i);
+          const int tw = __shfl_sync(0xffffffffu, cur.two, i);
           int good = 1;
           if (lane == 0) {
             if (r != cur_row) {
@@ -233,18 +257,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tma_load_2d(s.q[qs], &tmap_q, &s.qfull[qs], 0, (p.row_base + r) * kHeads, pol_q);
               }
             }
-            if (good && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs))
-              good = 0;
+            if (good && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs)) good = 0;
+            if (good && !mbar_wait(&s.sempty[sslot], sphase ^ 1u, &s.abort, kWaitTimeoutNs)) good = 0;
             if (good) {
-              mbar_arrive_expect_tx(&s.full[stage], tw ? 2 * kPageTxBytes : kPageTxBytes);
+              mbar_arrive_expect_tx(&s.full[stage], tw ? 2 * kPageKBytes : kPageKBytes);
+              mbar_arrive_expect_tx(&s.sfull[sslot], tw ? 2 * kScaleTx : kScaleTx);
               tma_load_3d(s.k[stage], &tmap_k, &s.full[stage], 0, 0, a, pol_k);
-              tma_load_2d(s.scale[stage], &tmap_s, &s.full[stage], 0, a, pol_k);
+              tma_load_2d(s.scale[sslot], &tmap_s, &s.sfull[sslot], 0, a, pol_k);
               if (tw) {
                 tma_load_3d(s.k[stage] + kPageKBytes, &tmap_k, &s.full[stage], 0, 0, b, pol_k);
-                tma_load_2d(s.scale[stage] + kPage, &tmap_s, &s.full[stage], 0, b, pol_k);
+                tma_load_2d(s.scale[sslot] + kPage, &tmap_s, &s.sfull[sslot], 0, b, pol_k);
               }
-              ++fills[stage];
+              ++k_fills;
+              ++s_fills;
               if (++stage == kStages) { stage = 0; phase ^= 1u; }
+              if (++sslot == kScaleSlots) { sslot = 0; sphase ^= 1u; }
             } else {
               fail(s, p.status);
             }
@@ -254,11 +281,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Never leave with a TMA in flight: wait for the latest fill of every
-      // stage and Q slot (all earlier fills were consumed, hence complete).
+      // slot (each earlier fill of a slot was consumed, hence complete).
       if (lane == 0) {
-        for (int i = 0; i < kStages; ++i)
-          if (fills[i] > 0 && !mbar_wait(&s.full[i], (fills[i] - 1) & 1, nullptr, kWaitTimeoutNs))
+        for (int i = 0; i < kStages && i < k_fills; ++i) {
+          const int last = k_fills - 1 - i;  // fill index of the i-th latest fill
+          if (!mbar_wait(&s.full[last % kStages], (last / kStages) & 1, nullptr, kWaitTimeoutNs))
             report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+        }
+        for (int i = 0; i < kScaleSlots && i < s_fills; ++i) {
+          const int last = s_fills - 1 - i;
+          if (!mbar_wait(&s.sfull[last % kScaleSlots], (last / kScaleSlots) & 1, nullptr, kWaitTimeoutNs))
+            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+        }
         for (int i = 0; i < 2; ++i)
           if (q_uses[i] > 0 && !mbar_wait(&s.qfull[i], (q_uses[i] - 1) & 1, nullptr, kWaitTimeoutNs))
             report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
@@ -290,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kDim / 32; ++kk)  // K = 32 e4m3 (32 B) per MMA
             umma_f8(d, adesc + 2u * kk, bdesc + 2u * kk, idesc, kk > 0 ? 1u : 0u);
-          umma_commit(&s.empty[stage]);
+          umma_commit(&s.empty[stage]);  // K stage free once these MMAs are done
           umma_commit(&s.tfull[acc]);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
           if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
@@ -304,10 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------------------ epilogue
       const int quad = warp & 3;              // TMEM lanes [32*quad, 32*quad+32)
       const int tok = quad * 32 + lane;       // token of the tile owned by this thread
-      int stage = 0, acc = 0, cur_row = -1, L = 0;
-      uint32_t phase = 0, aphase = 0;
+      int acc = 0, sslot = 0, cur_row = -1, L = 0;
+      uint32_t aphase = 0, sphase = 0;
+      bool hist_row = false;
       float w[kHeads];
       float* out_row = nullptr;
+      uint32_t* hist_g = nullptr;
       Cursor c;
       c.init(rs, p.rows, t0);
       for (; c.t < t1; c.next(rs, t1)) {
@@ -320,9 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
           }
           L = row_len(p.seq_lens, cur_row, p.max_pages, nullptr);
+          hist_row = L > kTopK;  // only rows that go through the radix select
           out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
+          hist_g = p.hist + static_cast<size_t>(cur_row) * kHistBins;
         }
-        if (!mbar_wait(&s.full[stage], phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
         if (!mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
         tc_fence_after();
         uint32_t r0[32], r1[32];
@@ -332,12 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(taddr + 32u, r1);
         tmem_wait_ld();
         tc_fence_before();
-        const float sc = s.scale[stage][tok];
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&s.tempty[acc]);
-          mbar_arrive(&s.empty[stage]);
-        }
+        if (lane == 0) mbar_arrive(&s.tempty[acc]);
+        if (!mbar_wait(&s.sfull[sslot], sphase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        const float sc = s.scale[sslot][tok];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.sempty[sslot]);
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
         for (int h = 0; h < 32; h += 4) {
@@ -353,10 +390,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           a2 = fmaf(fmaxf(__uint_as_float(r1[h + 2]), 0.f), w[32 + h + 2], a2);
           a3 = fmaf(fmaxf(__uint_as_float(r1[h + 3]), 0.f), w[32 + h + 3], a3);
         }
+        const float logit = ((a0 + a1) + (a2 + a3)) * sc;
         const int t_abs = c.j * kTileTok + tok;
-        if (t_abs < L) out_row[t_abs] = ((a0 + a1) + (a2 + a3)) * sc;
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        if (t_abs < L) {
+          out_row[t_abs] = logit;
+          if (hist_row) atomicAdd(hist_g + (ordered_key(logit) >> (32 - kHistBits)), 1u);  // RED
+        }
         if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
+        if (++sslot == kScaleSlots) { sslot = 0; sphase ^= 1u; }
       }
     }
   }
@@ -390,6 +431,7 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   p.seq_lens = lp.seq_lens;
   p.block_table = lp.block_table;
   p.logits = lp.logits;
+  p.hist = lp.hist;
   p.status = lp.status;
   p.rows = lp.rows;
   p.max_pages = lp.max_pages;

@@ -3,21 +3,23 @@
 //
 // Keys are the order-preserving u32 image of the fp32 logit, so "top-K by
 // value" is "top-K by key".  Per row (one 1024-thread CTA):
-//   pass 1  histogram of the top 12 key bits (4096 bins) over all tokens,
-//           keys cached in shared memory when the row fits (<= 40960 tokens);
-//           the bin holding the K-th largest key is found by a block suffix
-//           scan;
-//   pass 2  tokens in higher bins are emitted directly; tokens in the pivot
-//           bin are compacted into a candidate list (<= 6144 entries, else
-//           the refinement below re-reads the row with a prefix filter);
-//   refine  10-bit + 10-bit histograms over the candidates give the exact
-//           32-bit pivot; candidates above it are emitted, and ties at the
-//           pivot fill the remaining slots in arbitrary order.
+//   digit 1  the histogram of the top 12 key bits (4096 bins) is the one the
+//            scoring kernel accumulated for the row; the bin holding the
+//            K-th largest key is found by a block suffix scan, and the
+//            histogram is cleared for the next call;
+//   pass     one vectorised pass over the row's logits: tokens in higher
+//            bins are emitted directly, tokens in the pivot bin are
+//            compacted into a shared-memory candidate list (<= 16384
+//            entries; beyond that the refinement re-reads the row with a
+//            prefix filter);
+//   refine   10-bit + 10-bit histograms over the candidates give the exact
+//            32-bit pivot; candidates above it are emitted, and ties at the
+//            pivot fill the remaining slots in arbitrary order.
 // Histogram updates are warp-aggregated with __match_any_sync (lanes holding
-// the same bin add once), output slots are taken with one atomic per warp
-// via __ballot_sync.  The emitted set is exactly a top-K set of the logits;
-// among equal logits at the boundary the choice is arbitrary, as in the
-// reference's atomic emit (solution/python/kernel.cu:992-1018).
+// the same bin add once), output slots are taken with one shared atomic per
+// warp (in-warp scan).  The emitted set is exactly a top-K set of the
+// logits; among equal logits at the boundary the choice is arbitrary, as in
+// the reference's atomic emit (solution/python/kernel.cu:992-1018).
 //
 // Rows with seq_len <= 2048 emit ids of tokens 0..L-1 in token order and -1
 // padding (reference kernel.cu:897-905, :1079-1097).
@@ -30,16 +32,14 @@ namespace dsai {
 namespace {
 
 constexpr int kThreads = 1024;
-constexpr int kBins1 = 4096;   // 12-bit first digit
 constexpr int kBins2 = 1024;   // 10-bit second and third digits
-constexpr int kCandCap = 6144;
-constexpr int kKeyCap = 40960;
+constexpr int kCandCap = 16384;
+constexpr int kUnroll = 4;     // float4 loads in flight per thread
 
 struct SelSmem {
-  uint32_t hist[kBins1];
+  uint32_t hist[kHistBins];
   uint32_t cand_key[kCandCap];
   int32_t cand_idx[kCandCap];
-  uint32_t keys[kKeyCap];
   int warp_tot[32];
   int sel_bin;
   int sel_above;
@@ -57,14 +57,21 @@ __device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool vali
   if ((threadIdx.x & 31) == (__ffs(peers) - 1)) atomicAdd(&hist[bin], __popc(peers));
 }
 
-// Warp-collective slot allocation: returns this lane's slot when pred holds.
-__device__ __forceinline__ int warp_alloc(int* counter, bool pred) {
+// Warp-collective slot allocation for `cnt` entries of this lane: returns the
+// first slot of this lane's entries (one shared atomic per warp).
+__device__ __forceinline__ int warp_alloc_n(int* counter, int cnt) {
   const int lane = threadIdx.x & 31;
-  const unsigned m = __ballot_sync(0xffffffffu, pred);
+  int incl = cnt;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  const int total = __shfl_sync(0xffffffffu, incl, 31);
   int base = 0;
-  if (lane == 0 && m) base = atomicAdd(counter, __popc(m));
-  base = __shfl_sync(0xffffffffu, base, 0);
-  return base + __popc(m & ((1u << lane) - 1u));
+  if (lane == 31 && total) base = atomicAdd(counter, total);
+  base = __shfl_sync(0xffffffffu, base, 31);
+  return base + incl - cnt;
 }
 
 // Finds the bin holding the k-th largest entry: sel_bin = bin with
@@ -76,8 +83,7 @@ __device__ void find_threshold(SelSmem& s, int nbins, int k) {
   const int lo = tid * per;
   int sum = 0;
   for (int i = 0; i < per; ++i) sum += s.hist[lo + i];
-  // inclusive suffix within the warp (higher lanes own higher bins)
-  int v = sum;
+  int v = sum;  // inclusive suffix within the warp (higher lanes own higher bins)
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
     const int y = __shfl_down_sync(0xffffffffu, v, off);
@@ -99,16 +105,13 @@ __device__ void find_threshold(SelSmem& s, int nbins, int k) {
   __syncthreads();
 }
 
-// Key source over one row of logits (key 0 never occurs for a finite or
-// infinite logit; it is used as "no entry").
+// Key sources.  key() == 0 means "no entry" (never produced for a real
+// logit: it is the image of one NaN bit pattern only).
 struct RowSrc {
   const float* row;
   __device__ __forceinline__ uint32_t key(int i) const { return ordered_key(row[i]); }
 };
-
-// Key source over a candidate list; padding (token -1) and tokens outside
-// the row [0, L) have key 0 and are never selected.
-struct CandSrc {
+struct CandSrc {  // (score, token) list; padding (token -1) or tokens >= L are no entry
   const float* scores;
   const int32_t* tokens;
   int L;
@@ -118,15 +121,15 @@ struct CandSrc {
   }
 };
 
-// Writes one selected entry: i is the source index, key its key.
-struct IdsOut {  // physical slot ids of tokens
+// Output writers: i is the source index, key its key.
+struct IdsOut {
   int32_t* out;
   const int32_t* bt_row;
   __device__ __forceinline__ void emit(int pos, int i, uint32_t) const {
     out[pos] = physical_id(bt_row, i);
   }
 };
-struct PairsOut {  // (score, token + offset)
+struct PairsOut {
   float* scores;
   int32_t* tokens;
   int32_t offset;
@@ -135,7 +138,7 @@ struct PairsOut {  // (score, token + offset)
     tokens[pos] = i + offset;
   }
 };
-struct MergeOut {  // physical slot ids of candidate tokens
+struct MergeOut {
   int32_t* out;
   const int32_t* bt_row;
   const int32_t* tokens;
@@ -144,13 +147,45 @@ struct MergeOut {  // physical slot ids of candidate tokens
   }
 };
 
-// Selects the kTopK largest keys among src[0, n) (at least kTopK valid).
-template <class Src, class Out>
-__device__ void select_topk(const Src& src, const Out& out, int n, SelSmem& s) {
-  const int tid = threadIdx.x;
-  const bool cached = n <= kKeyCap;
+// Emits keys above the pivot bin and compacts the pivot bin, for up to 4
+// consecutive entries i0.. of this thread (cnt of them valid).
+template <class Out>
+__device__ __forceinline__ void classify(SelSmem& s, const Out& out, const uint32_t (&key)[4],
+                                         int i0, int cnt, uint32_t bin1, bool use_cand) {
+  int ngt = 0, neq = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (u < cnt && key[u] != 0u) {
+      const uint32_t b = key[u] >> (32 - kHistBits);
+      ngt += b > bin1;
+      neq += (use_cand && b == bin1);
+    }
+  }
+  int pos = warp_alloc_n(&s.out_count, ngt);
+  int cpos = warp_alloc_n(&s.cand_count, neq);
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (u < cnt && key[u] != 0u) {
+      const uint32_t b = key[u] >> (32 - kHistBits);
+      if (b > bin1) {
+        out.emit(pos++, i0 + u, key[u]);
+      } else if (use_cand && b == bin1) {
+        s.cand_key[cpos] = key[u];
+        s.cand_idx[cpos] = i0 + u;
+        ++cpos;
+      }
+    }
+  }
+}
 
-  for (int i = tid; i < kBins1; i += kThreads) s.hist[i] = 0u;
+// Selects the kTopK largest keys among src[0, n) (at least kTopK entries).
+// g_hist: the 12-bit histogram of the entries accumulated by the producer of
+// src (cleared here), or null to compute it.  VEC: the source is the 16-B
+// aligned float row `row`, read with float4 loads.
+template <bool VEC, class Src, class Out>
+__device__ void select_topk(const Src& src, const float* row, const Out& out, int n,
+                            uint32_t* g_hist, SelSmem& s) {
+  const int tid = threadIdx.x;
   if (tid == 0) {
     s.out_count = 0;
     s.cand_count = 0;
@@ -158,53 +193,70 @@ __device__ void select_topk(const Src& src, const Out& out, int n, SelSmem& s) {
     s.sel_bin = 0;
     s.sel_above = 0;
   }
-  __syncthreads();
-
-  // pass 1: 12-bit histogram
-  for (int base = 0; base < n; base += kThreads) {
-    const int i = base + tid;
-    uint32_t key = 0u;
-    if (i < n) {
-      key = src.key(i);
-      if (cached) s.keys[i] = key;
+  if (g_hist) {
+    for (int i = tid; i < kHistBins; i += kThreads) {
+      s.hist[i] = g_hist[i];
+      g_hist[i] = 0u;
     }
-    hist_add(s.hist, key >> 20, key != 0u);
+    __syncthreads();
+  } else {
+    for (int i = tid; i < kHistBins; i += kThreads) s.hist[i] = 0u;
+    __syncthreads();
+    for (int base = 0; base < n; base += kThreads) {
+      const int i = base + tid;
+      const uint32_t key = i < n ? src.key(i) : 0u;
+      hist_add(s.hist, key >> (32 - kHistBits), key != 0u);
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  find_threshold(s, kBins1, kTopK);
+  find_threshold(s, kHistBins, kTopK);
   const uint32_t bin1 = static_cast<uint32_t>(s.sel_bin);
   const int k1 = kTopK - s.sel_above;
   const int n1 = static_cast<int>(s.hist[bin1]);
   const bool use_cand = n1 <= kCandCap;
 
-  // pass 2: emit above the pivot bin, compact the pivot bin
-  for (int base = 0; base < n; base += kThreads) {
-    const int i = base + tid;
-    uint32_t key = 0u;
-    if (i < n) key = cached ? s.keys[i] : src.key(i);
-    const uint32_t b = key >> 20;
-    const bool gt = key != 0u && b > bin1;
-    const bool eq = use_cand && key != 0u && b == bin1;
-    const int pos = warp_alloc(&s.out_count, gt);
-    if (gt) out.emit(pos, i, key);
-    const int cpos = warp_alloc(&s.cand_count, eq);
-    if (eq) {
-      s.cand_key[cpos] = key;
-      s.cand_idx[cpos] = i;
+  // One pass: emit above the pivot bin, compact the pivot bin.
+  if constexpr (VEC) {
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    const int n4 = n >> 2;
+    for (int base = 0; base < n4; base += kThreads * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int j = base + u * kThreads + tid;
+        v[u] = j < n4 ? __ldcs(row4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int j = base + u * kThreads + tid;
+        const uint32_t key[4] = {ordered_key(v[u].x), ordered_key(v[u].y), ordered_key(v[u].z),
+                                 ordered_key(v[u].w)};
+        classify(s, out, key, 4 * j, j < n4 ? 4 : 0, bin1, use_cand);
+      }
+    }
+    // tail: the last n % 4 entries
+    const int i = 4 * n4 + tid;
+    const uint32_t key[4] = {tid < (n & 3) ? ordered_key(row[i]) : 0u, 0u, 0u, 0u};
+    classify(s, out, key, i, tid < (n & 3) ? 1 : 0, bin1, use_cand);
+  } else {
+    for (int base = 0; base < n; base += kThreads) {
+      const int i = base + tid;
+      const uint32_t key[4] = {i < n ? src.key(i) : 0u, 0u, 0u, 0u};
+      classify(s, out, key, i, i < n ? 1 : 0, bin1, use_cand);
     }
   }
   __syncthreads();
 
-  // Entries of the pivot bin: the candidate list, or the row re-read.
+  // Entries of the pivot bin: the candidate list, or the source re-read.
   const int m = use_cand ? n1 : n;
   auto bucket = [&](int j, uint32_t& key, int& idx) {
     if (use_cand) {
       key = s.cand_key[j];
       idx = s.cand_idx[j];
     } else {
-      key = cached ? s.keys[j] : src.key(j);
+      key = src.key(j);
       idx = j;
-      if (key == 0u || (key >> 20) != bin1) key = 0u;
+      if (key == 0u || (key >> (32 - kHistBits)) != bin1) key = 0u;
     }
   };
 
@@ -246,9 +298,9 @@ __device__ void select_topk(const Src& src, const Out& out, int n, SelSmem& s) {
     if (j < m) bucket(j, key, idx);
     const bool gt = key != 0u && key > pivot;
     const bool eq = key != 0u && key == pivot;
-    const int pos = warp_alloc(&s.out_count, gt);
+    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
     if (gt) out.emit(pos, idx, key);
-    const int ticket = warp_alloc(&s.eq_count, eq);
+    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
     if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, idx, key);
   }
   __syncthreads();
@@ -261,6 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
   const float* row = p.logits + static_cast<size_t>(b) * p.ld;
+  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistBins;
 
   if (p.out_ids) {
     int32_t* out = p.out_ids + static_cast<size_t>(b) * kTopK;
@@ -268,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
       for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
       return;
     }
-    select_topk(RowSrc{row}, IdsOut{out, bt_row}, L, s);
+    select_topk<true>(RowSrc{row}, row, IdsOut{out, bt_row}, L, g_hist, s);
   } else {
     float* sc = p.out_scores + static_cast<size_t>(b) * kTopK;
     int32_t* tk = p.out_tokens + static_cast<size_t>(b) * kTopK;
@@ -279,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
       }
       return;
     }
-    select_topk(RowSrc{row}, PairsOut{sc, tk, p.token_offset}, L, s);
+    select_topk<true>(RowSrc{row}, row, PairsOut{sc, tk, p.token_offset}, L, g_hist, s);
   }
 }
 
@@ -296,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Slots stay -1 if the candidates hold fewer than kTopK real entries.
   for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = -1;
   __syncthreads();
-  select_topk(CandSrc{scores, tokens, L}, MergeOut{out, bt_row, tokens}, n_cand, s);
+  select_topk<false>(CandSrc{scores, tokens, L}, nullptr, MergeOut{out, bt_row, tokens}, n_cand,
+                     nullptr, s);
 }
 
 // Rows that all fit in the top-K (max_pages * 64 <= 2048): the output is the

@@ -78,12 +78,15 @@ typedef struct dsai_args {
 } dsai_args;
 
 /* Bytes of device workspace dsai_run needs for these sizes (256-B aligned
- * base required).  Replaces the reference's per-device fp16 logits scratch
- * (solution/python/kernel.cu:1299-1323). */
+ * base required): a status header, one 4096-bin histogram per row and the
+ * fp32 logits.  Replaces the reference's per-device fp16 logits scratch
+ * (solution/python/kernel.cu:1299-1323).  A workspace serves one call at a
+ * time: calls that may overlap on the GPU need separate workspaces. */
 DSAI_API size_t dsai_workspace_size(int32_t rows, int32_t max_pages);
 
-/* Zero the workspace header (status word).  Call once after allocating a
- * workspace; the header is sticky between calls otherwise. */
+/* Zero a workspace (status word and histograms).  Call once after
+ * allocating it; every call leaves the histograms zero again, and the status
+ * word is sticky until dsai_read_status. */
 DSAI_API int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /* The indexer, destination-passing.  Replaces the reference's extension op

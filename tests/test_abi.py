@@ -39,9 +39,10 @@ def test_only_the_api_is_exported(dsai_lib):
 
 
 def test_workspace_size(dsai_lib):
+    # header + one 4096-bin u32 histogram per row + fp32 logits (256-B rounded)
     assert dsai_lib.dsai_workspace_size(0, 0) == 256
-    assert dsai_lib.dsai_workspace_size(64, 512) == 256 + 64 * 512 * 64 * 4
-    assert dsai_lib.dsai_workspace_size(3, 5) == 256 + ((3 * 5 * 64 * 4 + 255) // 256) * 256
+    assert dsai_lib.dsai_workspace_size(64, 512) == 256 + 64 * 16384 + 64 * 512 * 64 * 4
+    assert dsai_lib.dsai_workspace_size(3, 5) == 256 + 3 * 16384 + ((3 * 5 * 64 * 4 + 255) // 256) * 256
     assert dsai_lib.dsai_workspace_size(-1, 4) == 0
 
 

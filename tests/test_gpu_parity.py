@@ -139,7 +139,7 @@ def test_many_ties_in_pivot_bucket(oracle_mod):
 def test_invalid_inputs_flagged_not_faulting(oracle_mod):
     inp = W.make_inputs([3000, 3000, 100], seed=26)
     bt = inp.block_table.clone()
-    bt[1, 5] = 1 << 30            # page out of range -> zero page, flagged
+    bt[1, 5] = inp.num_pages + 1000  # page out of range -> zero page, flagged
     inp.block_table = bt
     sl = inp.seq_lens.clone()
     sl[2] = 1 << 30               # clamped to max_pages*64, flagged

@@ -25,7 +25,7 @@ constexpr int kQBytes = kHeads * kDim;        // 8192 B of Q per row
 
 // Rows handled by one scoring launch (the per-CTA row table lives in smem);
 // the host splits larger batches into several launches.
-constexpr int kMaxRowsPerLaunch = 4096;
+constexpr int kMaxRowsPerLaunch = 1024;
 
 // First radix digit of the selection: the top 12 bits of the ordered key
 // (sign, 8 exponent bits, 3 mantissa bits).  The scorer builds a per-row

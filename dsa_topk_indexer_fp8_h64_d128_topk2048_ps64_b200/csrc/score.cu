@@ -13,9 +13,10 @@
 // [c*T/G, (c+1)*T/G), so every CTA moves the same number of K bytes and
 // crosses at most a few row boundaries (Q is reloaded only there).
 //
-// One CTA per SM, 6 warps, warp-specialised:
+// Two CTAs per SM (two independent pipelines per SM overlap each other's
+// latencies), 6 warps each, warp-specialised:
 //   warp 0      producer: follows block_table and TMA-loads each page (8 KB,
-//               128-B swizzle) into a 10-stage K ring, its 64 scales into a
+//               128-B swizzle) into a 5-stage K ring, its 64 scales into a
 //               16-slot scale ring, and the row's Q (8 KB) into a 2-slot ring.
 //               The 32 lanes resolve the pages of 32 tiles at once, one batch
 //               ahead, so the block-table pointer chase never stalls issue.
@@ -38,7 +39,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kStages = 10;
+constexpr int kCtasPerSm = 2;                  // two independent pipelines per SM
+constexpr int kStages = 5;
 constexpr int kScaleSlots = 16;
 constexpr int kAccs = 4;
 constexpr int kAccCols = kHeads;               // 64 fp32 columns per accumulator
@@ -82,7 +84,7 @@ struct ScoreSmem {
 };
 
 constexpr int kSmemBytes = static_cast<int>(sizeof(ScoreSmem)) + 1024;
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 233472, "two CTAs per SM must fit");
 
 // Last row r with row_start[r] <= t (t < row_start[rows]); that row is the
 // non-empty row holding tile t.
@@ -167,7 +169,7 @@ __device__ __forceinline__ TileRef resolve_tile(const ScoreSmem& s, const ScoreP
   return r;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     score_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_s, const ScoreParams p) {
@@ -176,6 +178,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  // Launched as a programmatic dependent: nothing before this point touches
+  // global memory, so the launch overlaps the previous kernel's tail.
+  sm100::grid_dep_wait();
+  sm100::grid_dep_launch_dependents();
   build_row_table(s, p);
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -439,8 +445,17 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   p.ld = lp.ld;
   p.row_base = lp.row_base;
   p.score_all = lp.score_all;
-  score_kernel<<<lp.grid, kThreads, kSmemBytes, stream>>>(tmap_q, tmap_k, tmap_s, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(lp.grid * kCtasPerSm);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, score_kernel, tmap_q, tmap_k, tmap_s, p);
 }
 
 }  // namespace dsai

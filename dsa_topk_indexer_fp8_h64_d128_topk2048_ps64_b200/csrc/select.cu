@@ -2,14 +2,14 @@
 // partial (score, token) candidate lists.
 //
 // Keys are the order-preserving u32 image of the fp32 logit, so "top-K by
-// value" is "top-K by key".  Per row (one 1024-thread CTA):
+// value" is "top-K by key".  Per row (one 512-thread CTA, two per SM):
 //   digit 1  the histogram of the top 12 key bits (4096 bins) is the one the
 //            scoring kernel accumulated for the row; the bin holding the
 //            K-th largest key is found by a block suffix scan, and the
 //            histogram is cleared for the next call;
 //   pass     one vectorised pass over the row's logits: tokens in higher
 //            bins are emitted directly, tokens in the pivot bin are
-//            compacted into a shared-memory candidate list (<= 16384
+//            compacted into a shared-memory candidate list (<= 8192
 //            entries; beyond that the refinement re-reads the row with a
 //            prefix filter);
 //   refine   10-bit + 10-bit histograms over the candidates give the exact
@@ -27,20 +27,29 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "sm100.cuh"
 
 namespace dsai {
 namespace {
 
-constexpr int kThreads = 1024;
+using sm100::grid_dep_launch_dependents;
+using sm100::grid_dep_wait;
+
+constexpr int kThreads = 512;
 constexpr int kBins2 = 1024;   // 10-bit second and third digits
-constexpr int kCandCap = 16384;
-constexpr int kUnroll = 4;     // float4 loads in flight per thread
+constexpr int kCandCap = 8192;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 8;     // float4 loads in flight per thread
+constexpr int kBtCache = 4096; // block-table entries of a row kept in smem (rows <= 262144 tokens)
 
 struct SelSmem {
+  int32_t bt[kBtCache];
   uint32_t hist[kHistBins];
   uint32_t cand_key[kCandCap];
   int32_t cand_idx[kCandCap];
   int warp_tot[32];
+  int warp_suf[32];
+  uint32_t scan_total;
   int sel_bin;
   int sel_above;
   int out_count;
@@ -76,13 +85,20 @@ __device__ __forceinline__ int warp_alloc_n(int* counter, int cnt) {
 
 // Finds the bin holding the k-th largest entry: sel_bin = bin with
 // above(bin) < k <= above(bin) + hist[bin], sel_above = above(bin), where
-// above(bin) counts entries in higher bins.  nbins is 4096 or 1024.
+// above(bin) counts entries in higher bins.  nbins is 4096 or 1024.  A
+// two-level shuffle suffix scan (lanes, then the 32 warp totals).
 __device__ void find_threshold(SelSmem& s, int nbins, int k) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int per = nbins / kThreads;
   const int lo = tid * per;
+  constexpr int kMaxPer = kHistBins / kThreads;
+  uint32_t h[kMaxPer];
   int sum = 0;
-  for (int i = 0; i < per; ++i) sum += s.hist[lo + i];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    h[i] = i < per ? s.hist[lo + i] : 0u;
+    sum += static_cast<int>(h[i]);
+  }
   int v = sum;  // inclusive suffix within the warp (higher lanes own higher bins)
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
@@ -91,18 +107,58 @@ __device__ void find_threshold(SelSmem& s, int nbins, int k) {
   }
   if (lane == 0) s.warp_tot[warp] = v;
   __syncthreads();
-  int warps_above = 0;
-  for (int w = warp + 1; w < kThreads / 32; ++w) warps_above += s.warp_tot[w];
-  int above = warps_above + (v - sum);
-  for (int i = per - 1; i >= 0; --i) {
-    const int h = s.hist[lo + i];
-    if (above < k && above + h >= k) {
-      s.sel_bin = lo + i;
-      s.sel_above = above;
+  if (warp == 0) {
+    int t = lane < kWarps ? s.warp_tot[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_down_sync(0xffffffffu, t, off);
+      if (lane + off < 32) t += y;
     }
-    above += h;
+    s.warp_suf[lane] = t;  // entries in warps >= lane
   }
   __syncthreads();
+  int above = (warp < kWarps - 1 ? s.warp_suf[warp + 1] : 0) + (v - sum);
+#pragma unroll
+  for (int i = kMaxPer - 1; i >= 0; --i) {
+    if (i < per) {
+      const int hi = static_cast<int>(h[i]);
+      if (above < k && above + hi >= k) {
+        s.sel_bin = lo + i;
+        s.sel_above = above;
+      }
+      above += hi;
+    }
+  }
+  __syncthreads();
+}
+
+// Block-wide exclusive scan of a packed pair of counts (low / high 16 bits;
+// the totals must stay below 65536).  Returns this thread's exclusive prefix
+// and writes the block total to *total.
+__device__ __forceinline__ uint32_t block_scan_packed(SelSmem& s, uint32_t v, uint32_t* total) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += y;
+  }
+  if (lane == 31) s.warp_tot[warp] = static_cast<int>(incl);
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t t = lane < kWarps ? static_cast<uint32_t>(s.warp_tot[lane]) : 0u;
+    uint32_t ti = t;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, ti, off);
+      if (lane >= off) ti += y;
+    }
+    s.warp_suf[lane] = static_cast<int>(ti - t);  // exclusive prefix of warp totals
+    if (lane == kWarps - 1) s.scan_total = ti;
+  }
+  __syncthreads();
+  *total = s.scan_total;
+  return static_cast<uint32_t>(s.warp_suf[warp]) + incl - v;
 }
 
 // Key sources.  key() == 0 means "no entry" (never produced for a real
@@ -194,10 +250,13 @@ __device__ void select_topk(const Src& src, const float* row, const Out& out, in
     s.sel_above = 0;
   }
   if (g_hist) {
-    for (int i = tid; i < kHistBins; i += kThreads) {
-      s.hist[i] = g_hist[i];
-      g_hist[i] = 0u;
-    }
+    static_assert(kHistBins == 8 * kThreads, "eight bins per thread");
+    uint4* g4 = reinterpret_cast<uint4*>(g_hist);
+    const uint4 h0 = g4[tid], h1 = g4[tid + kThreads];  // both loads in flight
+    reinterpret_cast<uint4*>(s.hist)[tid] = h0;
+    reinterpret_cast<uint4*>(s.hist)[tid + kThreads] = h1;
+    g4[tid] = make_uint4(0u, 0u, 0u, 0u);  // clean for the next call
+    g4[tid + kThreads] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
   } else {
     for (int i = tid; i < kHistBins; i += kThreads) s.hist[i] = 0u;
@@ -215,29 +274,59 @@ __device__ void select_topk(const Src& src, const float* row, const Out& out, in
   const int n1 = static_cast<int>(s.hist[bin1]);
   const bool use_cand = n1 <= kCandCap;
 
-  // One pass: emit above the pivot bin, compact the pivot bin.
+  // One pass: emit above the pivot bin, compact the pivot bin.  Each chunk
+  // gives every thread 32 consecutive-in-float4 entries; they are classified
+  // into two bit masks (above the pivot bin / in it), the output slots come
+  // from one block-wide scan of the mask popcounts, and only the set bits
+  // (a few percent of the entries) are visited again, re-read through L1.
   if constexpr (VEC) {
+    constexpr int kPer = 4 * kUnroll;  // entries per thread per chunk (32)
+    static_assert(kPer == 32, "one mask bit per entry");
     const float4* row4 = reinterpret_cast<const float4*>(row);
-    const int n4 = n >> 2;
-    for (int base = 0; base < n4; base += kThreads * kUnroll) {
+    const int n4 = (n + 3) >> 2;       // the row buffer is padded to a multiple of 4
+    int out_base = 0, cand_base = 0;
+    for (int base4 = 0; base4 < n4; base4 += kThreads * kUnroll) {
       float4 v[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        const int j = base + u * kThreads + tid;
-        v[u] = j < n4 ? __ldcs(row4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int j = base4 + u * kThreads + tid;
+        v[u] = j < n4 ? row4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      uint32_t gtm = 0u, eqm = 0u;
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        const int j = base + u * kThreads + tid;
-        const uint32_t key[4] = {ordered_key(v[u].x), ordered_key(v[u].y), ordered_key(v[u].z),
-                                 ordered_key(v[u].w)};
-        classify(s, out, key, 4 * j, j < n4 ? 4 : 0, bin1, use_cand);
+        const int i0 = 4 * (base4 + u * kThreads + tid);
+        const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t b = ordered_key(x[c]) >> (32 - kHistBits);
+          const bool in = i0 + c < n;
+          gtm |= static_cast<uint32_t>(in && b > bin1) << (4 * u + c);
+          eqm |= static_cast<uint32_t>(in && use_cand && b == bin1) << (4 * u + c);
+        }
       }
+      uint32_t tot;
+      const uint32_t pre = block_scan_packed(s, __popc(gtm) | (__popc(eqm) << 16), &tot);
+      int pos = out_base + static_cast<int>(pre & 0xFFFFu);
+      int cpos = cand_base + static_cast<int>(pre >> 16);
+      uint32_t m = gtm | eqm;
+      while (m) {
+        const int e = __ffs(m) - 1;
+        m &= m - 1u;
+        const int i = 4 * (base4 + (e >> 2) * kThreads + tid) + (e & 3);
+        const uint32_t key = ordered_key(row[i]);  // L1 hit: loaded just above
+        if ((gtm >> e) & 1u) {
+          out.emit(pos++, i, key);
+        } else {
+          s.cand_key[cpos] = key;
+          s.cand_idx[cpos] = i;
+          ++cpos;
+        }
+      }
+      out_base += static_cast<int>(tot & 0xFFFFu);
+      cand_base += static_cast<int>(tot >> 16);
     }
-    // tail: the last n % 4 entries
-    const int i = 4 * n4 + tid;
-    const uint32_t key[4] = {tid < (n & 3) ? ordered_key(row[i]) : 0u, 0u, 0u, 0u};
-    classify(s, out, key, i, tid < (n & 3) ? 1 : 0, bin1, use_cand);
+    if (tid == 0) s.out_count = out_base;
   } else {
     for (int base = 0; base < n; base += kThreads) {
       const int i = base + tid;
@@ -309,6 +398,10 @@ __device__ void select_topk(const Src& src, const float* row, const Out& out, in
 __global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   SelSmem& s = *reinterpret_cast<SelSmem*>(smem_raw);
+  // Launched as a programmatic dependent of the scoring kernel: wait for its
+  // logits and histograms, then let the next grid start launching.
+  grid_dep_wait();
+  grid_dep_launch_dependents();
   const int b = blockIdx.x;
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
@@ -321,7 +414,15 @@ __global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
       for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
       return;
     }
-    select_topk<true>(RowSrc{row}, row, IdsOut{out, bt_row}, L, g_hist, s);
+    // The row's block table in shared memory: emitting an id then costs no
+    // dependent global load.
+    const int npages = (L + kPage - 1) / kPage;
+    const int32_t* bt_ids = bt_row;
+    if (npages <= kBtCache) {
+      for (int i = threadIdx.x; i < npages; i += kThreads) s.bt[i] = bt_row[i];
+      bt_ids = s.bt;  // made visible by the barrier inside select_topk
+    }
+    select_topk<true>(RowSrc{row}, row, IdsOut{out, bt_ids}, L, g_hist, s);
   } else {
     float* sc = p.out_scores + static_cast<size_t>(b) * kTopK;
     int32_t* tk = p.out_tokens + static_cast<size_t>(b) * kTopK;
@@ -398,8 +499,17 @@ cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
   cudaError_t e = ensure_attrs();
   if (e != cudaSuccess) return e;
   if (p.rows <= 0) return cudaSuccess;
-  select_kernel<<<p.rows, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.rows);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, select_kernel, p);
 }
 
 cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,

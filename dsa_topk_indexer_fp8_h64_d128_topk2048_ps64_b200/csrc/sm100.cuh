@@ -73,6 +73,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   }
 }
 
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (a no-op when the kernel was not
+// launched as a dependent), and allow the next grid to begin launching.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 3-D tiled tensor load into shared memory, completion counted in bytes on
 // `bar`.  The tensor map lives in kernel parameter space (__grid_constant__).
@@ -110,6 +120,24 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// 16-byte asynchronous global->shared copy (L2 only); src_bytes = 0 reads
+// nothing and zero-fills the destination.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Arrive on `bar` once every cp.async issued so far by this thread has
+// landed; the arrival counts toward the barrier's expected count.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05

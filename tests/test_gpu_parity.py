@@ -99,7 +99,7 @@ def test_all_short_rows_fast_path(oracle_mod):
 
 
 def test_long_rows_beyond_smem_cache(oracle_mod):
-    """Rows longer than the select kernel's shared-memory key cache (40960)."""
+    """Long rows: several selection chunks and a large pivot bin."""
     inp = W.make_inputs([45000, 70001], seed=23)
     ids, glog, status = gpu_run(inp)
     assert status == 0
@@ -198,11 +198,11 @@ def test_config1_full_size_properties(oracle_mod):
 
 
 def test_row_chunking_over_launch_limit(oracle_mod):
-    """More rows than one scoring launch handles (4096)."""
+    """More rows than one scoring launch handles (1024): five launches."""
     rows = 4100
     lens = np.full(rows, 2100)
     lens[::97] = 3000
     inp = W.make_inputs(lens, seed=27)
     ids, glog, status = gpu_run(inp, score_all=False)
     assert status == 0
-    check(oracle_mod, inp, ids, glog, rows=[0, 1, 4095, 4096, 4099])
+    check(oracle_mod, inp, ids, glog, rows=[0, 1, 1023, 1024, 2048, 4095, 4096, 4099])

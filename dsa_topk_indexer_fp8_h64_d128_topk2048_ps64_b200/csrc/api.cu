@@ -256,6 +256,10 @@ int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, 
 
 }  // namespace
 
+namespace dsai {
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace dsai
+
 extern "C" {
 
 size_t dsai_workspace_size(int32_t rows, int32_t max_pages) {

@@ -54,6 +54,9 @@ cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
                          const int32_t* bt_row, int max_pages, const int32_t* seq_len,
                          int32_t* out, cudaStream_t stream);
 
+// Records `msg` as the calling thread's dsai_last_error() and returns code.
+int set_last_error(int code, const char* msg);
+
 int score_smem_bytes();
 int select_smem_bytes();
 

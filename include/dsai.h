@@ -114,6 +114,19 @@ DSAI_API int dsai_merge_pairs(const float* scores, const int32_t* tokens, int32_
                      const int32_t* bt_row, int32_t max_pages,
                      const int32_t* seq_len, int32_t* out, void* stream);
 
+/* The indexer for callers that cannot allocate device memory (a host that
+ * owns all device allocations and forbids plugins to call cudaMalloc, a
+ * serving loop that bans allocation after warm-up, a binding without a
+ * device allocator).  Same arguments and results as dsai_run, but no
+ * workspace: it uses a 16 MiB device array built into the library, held on
+ * every GPU that loads it until the process exits.  Calls needing more than
+ * 16 MiB of workspace (dsai_workspace_size) fail with DSAI_E_WORKSPACE.
+ * The first call on a device looks up and zeroes the array (make it before
+ * any stream capture).  All calls on a device share the array: calls whose
+ * work can overlap on the GPU race and must be serialised.  No counterpart
+ * in the reference. */
+DSAI_API int dsai_run_noalloc(const dsai_args* args, void* stream);
+
 /* Copy the workspace status word to *status_out (host), then clear it.
  * Synchronises `stream`. */
 DSAI_API int dsai_read_status(void* workspace, void* stream, int32_t* status_out);

@@ -91,3 +91,12 @@ def test_python_entry_validates_like_the_reference():
     out = torch.zeros((2, 2048), dtype=torch.int32)
     with pytest.raises(RuntimeError, match="block_table must be int32 contiguous CUDA"):
         kernel(None, None, None, sl, bt, out)
+
+
+def test_noalloc_rejects_without_device(dsai_lib):
+    """The allocation-free entry point checks its arguments and its size
+    limit before it touches the device."""
+    assert dsai_lib.dsai_run_noalloc(None, None) == -1
+    a = _args(rows=256, max_pages=2048, num_pages=1)  # far more than its 16 MiB array
+    assert dsai_lib.dsai_run_noalloc(ctypes.byref(a), None) == -2
+    assert b"static scratch" in dsai_lib.dsai_last_error()

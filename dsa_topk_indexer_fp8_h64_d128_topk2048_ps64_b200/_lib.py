@@ -30,7 +30,7 @@ FLAG_SCORE_ALL_ROWS = 0x1
 EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
     "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
-    "dsai_run_noalloc",
+    "dsai_run_noalloc", "dsai_selftest_wait_timeout",
 )
 
 
@@ -81,6 +81,8 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.dsai_merge_pairs.restype = ctypes.c_int
         lib.dsai_run_noalloc.argtypes = [ctypes.POINTER(DsaiArgs), vp]
         lib.dsai_run_noalloc.restype = ctypes.c_int
+        lib.dsai_selftest_wait_timeout.argtypes = [vp, ctypes.c_uint64, vp]
+        lib.dsai_selftest_wait_timeout.restype = ctypes.c_int
         lib.dsai_read_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
         lib.dsai_read_status.restype = ctypes.c_int
         lib.dsai_last_error.argtypes = []

@@ -394,6 +394,18 @@ int dsai_read_status(void* workspace, void* stream_, int32_t* status_out) {
   return DSAI_OK;
 }
 
+int dsai_selftest_wait_timeout(void* workspace, uint64_t timeout_ns, void* stream) {
+  if (!workspace) return fail(DSAI_E_INVALID, "workspace is NULL");
+  if (timeout_ns == 0 || timeout_ns > dsai::kWaitTimeoutNs) return fail(DSAI_E_INVALID, "timeout out of range");
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  cudaError_t e = dsai::launch_wait_selftest(static_cast<int*>(workspace), timeout_ns,
+                                             static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "self-test kernel launch");
+  return DSAI_OK;
+}
+
 const char* dsai_last_error(void) { return g_err; }
 
 const char* dsai_version(void) { return "dsai 0.1.0 (sm_100a)"; }

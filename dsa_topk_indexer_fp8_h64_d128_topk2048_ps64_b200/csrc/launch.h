@@ -50,6 +50,8 @@ cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream);
 cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,
                               int max_pages, int32_t* out, cudaStream_t stream);
 
+cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream);
+
 cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
                          const int32_t* bt_row, int max_pages, const int32_t* seq_len,
                          int32_t* out, cudaStream_t stream);

@@ -476,6 +476,20 @@ __global__ void __launch_bounds__(128) short_rows_kernel(const int32_t* seq_lens
   }
 }
 
+// Self-test of the bounded on-chip waits: waits on an mbarrier that nothing
+// completes; the wait gives up after timeout_ns and reports
+// DSAI_STATUS_WAIT_TIMEOUT, exactly as the indexer kernels do.
+__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long timeout_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !sm100::mbar_wait(&bar, 0, nullptr, timeout_ns))
+    report(status, DSAI_STATUS_WAIT_TIMEOUT);
+}
+
 bool g_attr_done[64];
 
 cudaError_t ensure_attrs() {
@@ -516,6 +530,11 @@ cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_tabl
                               int max_pages, int32_t* out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
   short_rows_kernel<<<rows, 128, 0, stream>>>(seq_lens, block_table, max_pages, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(status, timeout_ns);
   return cudaGetLastError();
 }
 

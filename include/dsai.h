@@ -131,6 +131,14 @@ DSAI_API int dsai_run_noalloc(const dsai_args* args, void* stream);
  * Synchronises `stream`. */
 DSAI_API int dsai_read_status(void* workspace, void* stream, int32_t* status_out);
 
+/* Self-test of failure detection: launches one kernel that waits on an
+ * on-chip barrier nothing will complete, bounded by timeout_ns (at most 1 s);
+ * the wait gives up and sets DSAI_STATUS_WAIT_TIMEOUT in the workspace status
+ * word, as a stalled indexer kernel would, and the context stays usable.
+ * Read the result with dsai_read_status.  No reference counterpart (the
+ * reference's waits spin without bound, solution/python/tcgen05_ptx.h:164-167). */
+DSAI_API int dsai_selftest_wait_timeout(void* workspace, uint64_t timeout_ns, void* stream);
+
 /* Message of the last failure on this thread ("" if none). */
 DSAI_API const char* dsai_last_error(void);
 

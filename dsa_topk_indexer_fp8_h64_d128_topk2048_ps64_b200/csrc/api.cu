@@ -323,6 +323,7 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   sp.out_scores = nullptr;
   sp.out_tokens = nullptr;
   sp.token_offset = 0;
+  sp.sms = dev.sms;
   cudaError_t e = dsai::launch_select(sp, stream);
   if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
   return DSAI_OK;
@@ -363,6 +364,7 @@ int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, 
   sp.out_scores = out_scores;
   sp.out_tokens = out_tokens;
   sp.token_offset = token_offset;
+  sp.sms = dev.sms;
   cudaError_t e = dsai::launch_select(sp, stream);
   if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
   return DSAI_OK;

@@ -43,7 +43,16 @@ struct SelectLaunch {
   float* out_scores;
   int32_t* out_tokens;
   int32_t token_offset;
+  int sms;              // SMs of the device (sizes the clusters)
 };
+
+// Shape of the selection launch: threads per CTA and CTAs per row (the
+// cluster size).
+struct SelectShape {
+  int threads;
+  int cluster;
+};
+SelectShape select_shape(int rows, int max_pages, int sms);
 
 cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream);
 

@@ -2,27 +2,53 @@
 // partial (score, token) candidate lists.
 //
 // Keys are the order-preserving u32 image of the fp32 logit, so "top-K by
-// value" is "top-K by key".  Per row (one 512-thread CTA, two per SM):
-//   digit 1  the histogram of the top 12 key bits (4096 bins) is the one the
-//            scoring kernel accumulated for the row; the bin holding the
-//            K-th largest key is found by a block suffix scan, and the
-//            histogram is cleared for the next call;
-//   pass     one vectorised pass over the row's logits: tokens in higher
-//            bins are emitted directly, tokens in the pivot bin are
-//            compacted into a shared-memory candidate list (<= 8192
-//            entries; beyond that the refinement re-reads the row with a
-//            prefix filter);
-//   refine   10-bit + 10-bit histograms over the candidates give the exact
-//            32-bit pivot; candidates above it are emitted, and ties at the
-//            pivot fill the remaining slots in arbitrary order.
-// Histogram updates are warp-aggregated with __match_any_sync (lanes holding
-// the same bin add once), output slots are taken with one shared atomic per
-// warp (in-warp scan).  The emitted set is exactly a top-K set of the
-// logits; among equal logits at the boundary the choice is arbitrary, as in
-// the reference's atomic emit (solution/python/kernel.cu:992-1018).
+// value" is "top-K by key".  A radix select over three digits (12, 10 and
+// 10 key bits) finds the exact 2048-th largest key (the pivot).  The first
+// digit's histogram (4096 bins per row) is accumulated by the scoring kernel
+// as it writes the logits.
+//
+// Many rows (select_wide_kernel): one 1024-thread CTA per row.
+//   digit 1  thread t reads bins [4t, 4t+4) of the row's histogram and a
+//            block suffix scan finds the bin holding the 2048-th largest key
+//            (the pivot bin), while the row's first 32768 logits are copied
+//            into shared memory;
+//   pass     32 entries per thread and round, one mask bit each: keys above
+//            the pivot bin go straight to the output, keys in it to a list in
+//            shared memory and to the histogram of their next 10 bits; slots
+//            come from one shared atomic per warp;
+//   refine   the second digit from that histogram; keys above the 22-bit
+//            prefix are emitted, and the few keys sharing it (at most 64;
+//            else a third digit is counted) are ranked by one warp, which
+//            fills the last slots (ties at the pivot in list order).
+//
+// Few long rows (select_rows_kernel): one thread-block cluster of C CTAs
+// per row (C = 2..8, so that every CTA is resident at once), 256 threads per
+// CTA, three CTAs per SM.
+//   digit 1  the leader CTA finds the pivot bin and hands it to the
+//            cluster's CTAs (distributed shared memory, one cluster barrier)
+//            while their first round of logits is copied into shared memory;
+//   pass     CTA r classifies its page-aligned segment of the row, 8192
+//            entries per round: keys above the pivot bin go straight to the
+//            output, at slots taken with one atomic per CTA and round on the
+//            leader CTA's counter; keys in the pivot bin are kept, with their
+//            output value, in the CTA's own list and counted in its histogram
+//            of the next 10 key bits;
+//   refine   after a cluster barrier the leader sums the CTAs' histograms to
+//            find the second digit, counts the third digit over the lists
+//            (read in place through distributed shared memory) and emits the
+//            keys above the exact pivot; keys equal to the pivot fill the last
+//            slots in arbitrary order.
+// If the pivot bin holds more keys than the lists keep (heavily tied
+// logits) the refinement runs over the row in global memory instead.  The
+// emitted set is exactly a top-K set of the logits; among equal logits at
+// the boundary the choice is arbitrary, as in the reference's atomic emit
+// (solution/python/kernel.cu:992-1018).
 //
 // Rows with seq_len <= 2048 emit ids of tokens 0..L-1 in token order and -1
 // padding (reference kernel.cu:897-905, :1079-1097).
+//
+// The merge of (score, token) lists from a page-range split runs the same
+// three digits in one 512-thread CTA over the list.
 #include <cfloat>
 
 #include "common.cuh"
@@ -35,29 +61,19 @@ namespace {
 using sm100::grid_dep_launch_dependents;
 using sm100::grid_dep_wait;
 
-constexpr int kThreads = 512;
 constexpr int kBins2 = 1024;   // 10-bit second and third digits
 constexpr int kCandCap = 8192;
-constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 8;     // float4 loads in flight per thread
-constexpr int kBtCache = 4096; // block-table entries of a row kept in smem (rows <= 262144 tokens)
 
-struct SelSmem {
-  int32_t bt[kBtCache];
-  uint32_t hist[kHistBins];
-  uint32_t cand_key[kCandCap];
-  int32_t cand_idx[kCandCap];
+// ------------------------------------------------------------ block helpers
+
+struct Scan {
   int warp_tot[32];
   int warp_suf[32];
-  uint32_t scan_total;
+  uint32_t total;
   int sel_bin;
   int sel_above;
-  int out_count;
-  int cand_count;
-  int eq_count;
+  int sel_count;
 };
-
-constexpr int kSmemBytes = static_cast<int>(sizeof(SelSmem));
 
 __device__ __forceinline__ void hist_add(uint32_t* hist, uint32_t bin, bool valid) {
   const unsigned active = __ballot_sync(0xffffffffu, valid);
@@ -83,51 +99,52 @@ __device__ __forceinline__ int warp_alloc_n(int* counter, int cnt) {
   return base + incl - cnt;
 }
 
-// Finds the bin holding the k-th largest entry: sel_bin = bin with
-// above(bin) < k <= above(bin) + hist[bin], sel_above = above(bin), where
-// above(bin) counts entries in higher bins.  nbins is 4096 or 1024.  A
-// two-level shuffle suffix scan (lanes, then the 32 warp totals).
-__device__ void find_threshold(SelSmem& s, int nbins, int k) {
+// Finds the bin holding the k-th largest entry of a histogram spread over
+// the block (thread t holds bins [t*PER, t*PER + PER) in h): sets sel_bin
+// to the bin with above(bin) < k <= above(bin) + count(bin), sel_above to
+// above(bin) (entries in higher bins) and sel_count to count(bin); all zero
+// if the histogram holds fewer than k entries.  A two-level shuffle suffix
+// scan (lanes, then the warp totals).  Ends with a block barrier.
+template <int NT, int PER>
+__device__ void find_threshold(Scan& sc, const uint32_t (&h)[PER], int k) {
+  constexpr int kW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = nbins / kThreads;
-  const int lo = tid * per;
-  constexpr int kMaxPer = kHistBins / kThreads;
-  uint32_t h[kMaxPer];
   int sum = 0;
 #pragma unroll
-  for (int i = 0; i < kMaxPer; ++i) {
-    h[i] = i < per ? s.hist[lo + i] : 0u;
-    sum += static_cast<int>(h[i]);
-  }
+  for (int i = 0; i < PER; ++i) sum += static_cast<int>(h[i]);
   int v = sum;  // inclusive suffix within the warp (higher lanes own higher bins)
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
     const int y = __shfl_down_sync(0xffffffffu, v, off);
     if (lane + off < 32) v += y;
   }
-  if (lane == 0) s.warp_tot[warp] = v;
+  if (lane == 0) sc.warp_tot[warp] = v;
+  if (tid == 0) {
+    sc.sel_bin = 0;
+    sc.sel_above = 0;
+    sc.sel_count = 0;
+  }
   __syncthreads();
   if (warp == 0) {
-    int t = lane < kWarps ? s.warp_tot[lane] : 0;
+    int t = lane < kW ? sc.warp_tot[lane] : 0;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int y = __shfl_down_sync(0xffffffffu, t, off);
       if (lane + off < 32) t += y;
     }
-    s.warp_suf[lane] = t;  // entries in warps >= lane
+    sc.warp_suf[lane] = t;  // entries in warps >= lane
   }
   __syncthreads();
-  int above = (warp < kWarps - 1 ? s.warp_suf[warp + 1] : 0) + (v - sum);
+  int above = (warp < kW - 1 ? sc.warp_suf[warp + 1] : 0) + (v - sum);
 #pragma unroll
-  for (int i = kMaxPer - 1; i >= 0; --i) {
-    if (i < per) {
-      const int hi = static_cast<int>(h[i]);
-      if (above < k && above + hi >= k) {
-        s.sel_bin = lo + i;
-        s.sel_above = above;
-      }
-      above += hi;
+  for (int i = PER - 1; i >= 0; --i) {
+    const int hi = static_cast<int>(h[i]);
+    if (above < k && above + hi >= k) {
+      sc.sel_bin = tid * PER + i;
+      sc.sel_above = above;
+      sc.sel_count = hi;
     }
+    above += hi;
   }
   __syncthreads();
 }
@@ -135,7 +152,9 @@ __device__ void find_threshold(SelSmem& s, int nbins, int k) {
 // Block-wide exclusive scan of a packed pair of counts (low / high 16 bits;
 // the totals must stay below 65536).  Returns this thread's exclusive prefix
 // and writes the block total to *total.
-__device__ __forceinline__ uint32_t block_scan_packed(SelSmem& s, uint32_t v, uint32_t* total) {
+template <int NT>
+__device__ __forceinline__ uint32_t block_scan_packed(Scan& sc, uint32_t v, uint32_t* total) {
+  constexpr int kW = NT / 32;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint32_t incl = v;
 #pragma unroll
@@ -143,315 +162,803 @@ __device__ __forceinline__ uint32_t block_scan_packed(SelSmem& s, uint32_t v, ui
     const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
     if (lane >= off) incl += y;
   }
-  if (lane == 31) s.warp_tot[warp] = static_cast<int>(incl);
+  if (lane == 31) sc.warp_tot[warp] = static_cast<int>(incl);
   __syncthreads();
   if (warp == 0) {
-    uint32_t t = lane < kWarps ? static_cast<uint32_t>(s.warp_tot[lane]) : 0u;
+    const uint32_t t = lane < kW ? static_cast<uint32_t>(sc.warp_tot[lane]) : 0u;
     uint32_t ti = t;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const uint32_t y = __shfl_up_sync(0xffffffffu, ti, off);
       if (lane >= off) ti += y;
     }
-    s.warp_suf[lane] = static_cast<int>(ti - t);  // exclusive prefix of warp totals
-    if (lane == kWarps - 1) s.scan_total = ti;
+    sc.warp_suf[lane] = static_cast<int>(ti - t);  // exclusive prefix of warp totals
+    if (lane == kW - 1) sc.total = ti;
   }
   __syncthreads();
-  *total = s.scan_total;
-  return static_cast<uint32_t>(s.warp_suf[warp]) + incl - v;
+  *total = sc.total;
+  return static_cast<uint32_t>(sc.warp_suf[warp]) + incl - v;
 }
 
-// Key sources.  key() == 0 means "no entry" (never produced for a real
-// logit: it is the image of one NaN bit pattern only).
-struct RowSrc {
-  const float* row;
-  __device__ __forceinline__ uint32_t key(int i) const { return ordered_key(row[i]); }
-};
-struct CandSrc {  // (score, token) list; padding (token -1) or tokens >= L are no entry
-  const float* scores;
-  const int32_t* tokens;
-  int L;
-  __device__ __forceinline__ uint32_t key(int i) const {
-    const int t = tokens[i];
-    return (t >= 0 && t < L) ? ordered_key(scores[i]) : 0u;
-  }
+// ------------------------------------------------------------ row selection
+
+constexpr int kCPer = 32;        // entries per thread per round (one mask bit each)
+constexpr int kCBtCache = 1024;  // block-table entries of a segment in smem
+constexpr int kMaxCluster = 8;
+
+// Shape of the cluster kernel (few long rows: C CTAs per row).
+template <int NT>
+struct SelShape;
+template <>
+struct SelShape<256> {
+  static constexpr int kCtasPerSm = 3;
+  static constexpr int kLocalCap = 4096;  // pivot-bin keys one CTA keeps
 };
 
-// Output writers: i is the source index, key its key.
-struct IdsOut {
-  int32_t* out;
-  const int32_t* bt_row;
-  __device__ __forceinline__ void emit(int pos, int i, uint32_t) const {
-    out[pos] = physical_id(bt_row, i);
-  }
+template <int NT>
+struct RowSmem {
+  static constexpr int kCap = SelShape<NT>::kLocalCap;
+  union {
+    uint4 hist1[kHistBins / 4];  // staging of the row's first-digit histogram
+    struct {
+      uint32_t key[kCap];        // this CTA's keys in the pivot bin and their
+      int32_t val[kCap];         // output values (physical id or token)
+    } cand;
+  } u;
+  float4 vals[kCPer / 4][NT];    // the current round's logits
+  uint32_t hist[kBins2];         // second-digit histogram of this CTA's keys
+  int32_t bt[kCBtCache];         // this CTA's pages of the row
+  Scan sc;
+  const uint32_t* cand_key_of[kMaxCluster];  // leader: every CTA's candidate lists
+  const int32_t* cand_val_of[kMaxCluster];
+  int gather_base[kMaxCluster + 1];          // leader: prefix of the CTAs' counts
+  int bcast[3];                  // the first digit, from the leader: bin, keys above, keys in it
+  int out_count;                 // leader: output slots taken (whole row)
+  int eq_count;                  // leader: pivot ties taken
+  int overflow;                  // leader: some CTA held more than kCap keys
+  int cand_count;                // keys this CTA holds
+  int base_out;                  // this CTA's first output slot of the current round
 };
-struct PairsOut {
+
+template <int NT>
+constexpr int row_smem_bytes() {
+  return static_cast<int>(sizeof(RowSmem<NT>));
+}
+static_assert(3 * (row_smem_bytes<256>() + 1024) <= 233472, "three 256-thread CTAs per SM must fit");
+
+template <bool kIds>
+struct RowOut {
+  int32_t* ids;
   float* scores;
   int32_t* tokens;
   int32_t offset;
-  __device__ __forceinline__ void emit(int pos, int i, uint32_t key) const {
-    scores[pos] = key_to_float(key);
-    tokens[pos] = i + offset;
-  }
-};
-struct MergeOut {
-  int32_t* out;
-  const int32_t* bt_row;
-  const int32_t* tokens;
-  __device__ __forceinline__ void emit(int pos, int i, uint32_t) const {
-    out[pos] = physical_id(bt_row, tokens[i]);
-  }
-};
-
-// Emits keys above the pivot bin and compacts the pivot bin, for up to 4
-// consecutive entries i0.. of this thread (cnt of them valid).
-template <class Out>
-__device__ __forceinline__ void classify(SelSmem& s, const Out& out, const uint32_t (&key)[4],
-                                         int i0, int cnt, uint32_t bin1, bool use_cand) {
-  int ngt = 0, neq = 0;
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    if (u < cnt && key[u] != 0u) {
-      const uint32_t b = key[u] >> (32 - kHistBits);
-      ngt += b > bin1;
-      neq += (use_cand && b == bin1);
-    }
-  }
-  int pos = warp_alloc_n(&s.out_count, ngt);
-  int cpos = warp_alloc_n(&s.cand_count, neq);
-#pragma unroll
-  for (int u = 0; u < 4; ++u) {
-    if (u < cnt && key[u] != 0u) {
-      const uint32_t b = key[u] >> (32 - kHistBits);
-      if (b > bin1) {
-        out.emit(pos++, i0 + u, key[u]);
-      } else if (use_cand && b == bin1) {
-        s.cand_key[cpos] = key[u];
-        s.cand_idx[cpos] = i0 + u;
-        ++cpos;
-      }
-    }
-  }
-}
-
-// Selects the kTopK largest keys among src[0, n) (at least kTopK entries).
-// g_hist: the 12-bit histogram of the entries accumulated by the producer of
-// src (cleared here), or null to compute it.  VEC: the source is the 16-B
-// aligned float row `row`, read with float4 loads.
-template <bool VEC, class Src, class Out>
-__device__ void select_topk(const Src& src, const float* row, const Out& out, int n,
-                            uint32_t* g_hist, SelSmem& s) {
-  const int tid = threadIdx.x;
-  if (tid == 0) {
-    s.out_count = 0;
-    s.cand_count = 0;
-    s.eq_count = 0;
-    s.sel_bin = 0;
-    s.sel_above = 0;
-  }
-  if (g_hist) {
-    static_assert(kHistBins == 8 * kThreads, "eight bins per thread");
-    uint4* g4 = reinterpret_cast<uint4*>(g_hist);
-    const uint4 h0 = g4[tid], h1 = g4[tid + kThreads];  // both loads in flight
-    reinterpret_cast<uint4*>(s.hist)[tid] = h0;
-    reinterpret_cast<uint4*>(s.hist)[tid + kThreads] = h1;
-    g4[tid] = make_uint4(0u, 0u, 0u, 0u);  // clean for the next call
-    g4[tid + kThreads] = make_uint4(0u, 0u, 0u, 0u);
-    __syncthreads();
-  } else {
-    for (int i = tid; i < kHistBins; i += kThreads) s.hist[i] = 0u;
-    __syncthreads();
-    for (int base = 0; base < n; base += kThreads) {
-      const int i = base + tid;
-      const uint32_t key = i < n ? src.key(i) : 0u;
-      hist_add(s.hist, key >> (32 - kHistBits), key != 0u);
-    }
-    __syncthreads();
-  }
-  find_threshold(s, kHistBins, kTopK);
-  const uint32_t bin1 = static_cast<uint32_t>(s.sel_bin);
-  const int k1 = kTopK - s.sel_above;
-  const int n1 = static_cast<int>(s.hist[bin1]);
-  const bool use_cand = n1 <= kCandCap;
-
-  // One pass: emit above the pivot bin, compact the pivot bin.  Each chunk
-  // gives every thread 32 consecutive-in-float4 entries; they are classified
-  // into two bit masks (above the pivot bin / in it), the output slots come
-  // from one block-wide scan of the mask popcounts, and only the set bits
-  // (a few percent of the entries) are visited again, re-read through L1.
-  if constexpr (VEC) {
-    constexpr int kPer = 4 * kUnroll;  // entries per thread per chunk (32)
-    static_assert(kPer == 32, "one mask bit per entry");
-    const float4* row4 = reinterpret_cast<const float4*>(row);
-    const int n4 = (n + 3) >> 2;       // the row buffer is padded to a multiple of 4
-    int out_base = 0, cand_base = 0;
-    for (int base4 = 0; base4 < n4; base4 += kThreads * kUnroll) {
-      float4 v[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int j = base4 + u * kThreads + tid;
-        v[u] = j < n4 ? row4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      uint32_t gtm = 0u, eqm = 0u;
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int i0 = 4 * (base4 + u * kThreads + tid);
-        const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t b = ordered_key(x[c]) >> (32 - kHistBits);
-          const bool in = i0 + c < n;
-          gtm |= static_cast<uint32_t>(in && b > bin1) << (4 * u + c);
-          eqm |= static_cast<uint32_t>(in && use_cand && b == bin1) << (4 * u + c);
-        }
-      }
-      uint32_t tot;
-      const uint32_t pre = block_scan_packed(s, __popc(gtm) | (__popc(eqm) << 16), &tot);
-      int pos = out_base + static_cast<int>(pre & 0xFFFFu);
-      int cpos = cand_base + static_cast<int>(pre >> 16);
-      uint32_t m = gtm | eqm;
-      while (m) {
-        const int e = __ffs(m) - 1;
-        m &= m - 1u;
-        const int i = 4 * (base4 + (e >> 2) * kThreads + tid) + (e & 3);
-        const uint32_t key = ordered_key(row[i]);  // L1 hit: loaded just above
-        if ((gtm >> e) & 1u) {
-          out.emit(pos++, i, key);
-        } else {
-          s.cand_key[cpos] = key;
-          s.cand_idx[cpos] = i;
-          ++cpos;
-        }
-      }
-      out_base += static_cast<int>(tot & 0xFFFFu);
-      cand_base += static_cast<int>(tot >> 16);
-    }
-    if (tid == 0) s.out_count = out_base;
-  } else {
-    for (int base = 0; base < n; base += kThreads) {
-      const int i = base + tid;
-      const uint32_t key[4] = {i < n ? src.key(i) : 0u, 0u, 0u, 0u};
-      classify(s, out, key, i, i < n ? 1 : 0, bin1, use_cand);
-    }
-  }
-  __syncthreads();
-
-  // Entries of the pivot bin: the candidate list, or the source re-read.
-  const int m = use_cand ? n1 : n;
-  auto bucket = [&](int j, uint32_t& key, int& idx) {
-    if (use_cand) {
-      key = s.cand_key[j];
-      idx = s.cand_idx[j];
+  // val: the physical id (kIds) or the token index of the entry.
+  __device__ __forceinline__ void emit(int pos, int32_t val, uint32_t key) const {
+    if constexpr (kIds) {
+      ids[pos] = val;
     } else {
-      key = src.key(j);
-      idx = j;
-      if (key == 0u || (key >> (32 - kHistBits)) != bin1) key = 0u;
+      scores[pos] = key_to_float(key);
+      tokens[pos] = val + offset;
     }
-  };
-
-  // refine: bits [10, 20)
-  for (int i = tid; i < kBins2; i += kThreads) s.hist[i] = 0u;
-  __syncthreads();
-  for (int base = 0; base < m; base += kThreads) {
-    const int j = base + tid;
-    uint32_t key = 0u;
-    int idx = 0;
-    if (j < m) bucket(j, key, idx);
-    hist_add(s.hist, (key >> 10) & 1023u, key != 0u);
   }
-  __syncthreads();
-  find_threshold(s, kBins2, k1);
-  const uint32_t bin2 = static_cast<uint32_t>(s.sel_bin);
-  const int k2 = k1 - s.sel_above;
-  const uint32_t prefix2 = (bin1 << 10) | bin2;
+};
 
-  // refine: bits [0, 10)
-  for (int i = tid; i < kBins2; i += kThreads) s.hist[i] = 0u;
-  __syncthreads();
-  for (int base = 0; base < m; base += kThreads) {
-    const int j = base + tid;
-    uint32_t key = 0u;
-    int idx = 0;
-    if (j < m) bucket(j, key, idx);
-    hist_add(s.hist, key & 1023u, key != 0u && (key >> 10) == prefix2);
-  }
-  __syncthreads();
-  find_threshold(s, kBins2, k2);
-  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sel_bin);
-  const int k3 = k2 - s.sel_above;  // how many keys equal to the pivot are taken
-
-  for (int base = 0; base < m; base += kThreads) {
-    const int j = base + tid;
-    uint32_t key = 0u;
-    int idx = 0;
-    if (j < m) bucket(j, key, idx);
-    const bool gt = key != 0u && key > pivot;
-    const bool eq = key != 0u && key == pivot;
-    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-    if (gt) out.emit(pos, idx, key);
-    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
-    if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, idx, key);
-  }
-  __syncthreads();
+// ordered_key in two integer instructions (arithmetic shift, xor).
+__device__ __forceinline__ uint32_t key_of_bits(uint32_t u) {
+  return u ^ (static_cast<uint32_t>(static_cast<int32_t>(u) >> 31) | 0x80000000u);
 }
 
-__global__ void __launch_bounds__(kThreads, 1) select_kernel(SelectLaunch p) {
+// Cross-CTA traffic (C > 1) is kept to a few bulk steps: the leader's first
+// digit handed to every CTA, one remote atomic per CTA and round (output
+// slots), the leader's reads of the other CTAs' counts, histograms and
+// candidate lists, and three cluster barriers.  (Per-key remote atomics or
+// stores into one CTA's shared memory serialise at that SM and cost
+// microseconds.)  With C = 1 the cluster barriers become block barriers.
+// Per entry the pass costs a handful of integer instructions; only entries
+// above or in the pivot bin are visited again.
+template <bool kIds, int NT>
+__global__ void __launch_bounds__(NT, SelShape<NT>::kCtasPerSm) select_rows_kernel(const SelectLaunch p) {
+  constexpr int kRound = NT * kCPer;
+  constexpr int kHistPer = kHistBins / NT;  // first-digit bins per thread
+  constexpr int kB2Per = kBins2 / NT;       // refinement bins per thread
+  constexpr int kCap = RowSmem<NT>::kCap;
+  static_assert(kHistPer % 4 == 0 && kB2Per >= 1, "bin ownership");
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  SelSmem& s = *reinterpret_cast<SelSmem*>(smem_raw);
+  RowSmem<NT>& s = *reinterpret_cast<RowSmem<NT>*>(smem_raw);
   // Launched as a programmatic dependent of the scoring kernel: wait for its
   // logits and histograms, then let the next grid start launching.
   grid_dep_wait();
   grid_dep_launch_dependents();
+  const int tid = threadIdx.x;
+  const int C = static_cast<int>(sm100::cluster_nctarank());
+  const int r = static_cast<int>(sm100::cluster_ctarank());
+  const int b = static_cast<int>(sm100::cluster_id_x());
+  const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
+  const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
+  const float* row = p.logits + static_cast<size_t>(b) * p.ld;
+  RowOut<kIds> out;
+  out.ids = kIds ? p.out_ids + static_cast<size_t>(b) * kTopK : nullptr;
+  out.scores = kIds ? nullptr : p.out_scores + static_cast<size_t>(b) * kTopK;
+  out.tokens = kIds ? nullptr : p.out_tokens + static_cast<size_t>(b) * kTopK;
+  out.offset = p.token_offset;
+
+  if (L <= kTopK) {
+    // Every token is selected; the cluster's CTAs share the 2048 slots.  No
+    // CTA of this cluster takes a cluster barrier on this path.
+    const int i1 = kTopK * (r + 1) / C;
+    for (int i = kTopK * r / C + tid; i < i1; i += NT) {
+      if constexpr (kIds) {
+        out.ids[i] = i < L ? physical_id(bt_row, i) : -1;
+      } else {
+        out.scores[i] = i < L ? row[i] : -INFINITY;
+        out.tokens[i] = i < L ? i + p.token_offset : -1;
+      }
+    }
+    return;
+  }
+
+  // Cluster barrier halves (block barriers for a single-CTA cluster).
+  auto arrive = [&](bool release) {
+    if (C > 1) {
+      if (release) sm100::cluster_arrive_release(); else sm100::cluster_arrive_relaxed();
+    }
+  };
+  auto wait = [&]() {
+    if (C > 1) sm100::cluster_wait_acquire(); else __syncthreads();
+  };
+
+  const bool leader = r == 0;
+  // Distributed shared memory is touched only after every CTA of the
+  // cluster is known to run (the matching wait).
+  arrive(false);
+  for (int i = tid; i < kBins2; i += NT) s.hist[i] = 0u;
+  if (tid == 0) {
+    s.out_count = 0;
+    s.eq_count = 0;
+    s.overflow = 0;
+    s.cand_count = 0;
+  }
+
+  // This CTA's segment [s0, s1) of the row: page-aligned, C segments cover it.
+  const int seg = ((L + C - 1) / C + kPage - 1) & ~(kPage - 1);
+  const int s0 = min(L, r * seg);
+  const int s1 = min(L, s0 + seg);
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  // One round of logits into shared memory (each thread copies, and later
+  // reads, its own 16-B pieces; the row buffer is padded to 64 entries).
+  // Pieces at or past s1 are neither read nor copied.
+  auto load_round = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) {
+      const int j = base / 4 + u * NT + tid;
+      if (4 * j < s1) sm100::cp_async_16(&s.vals[u][tid], row4 + j, 16u);
+    }
+  };
+  if (s0 < s1) load_round(s0);
+
+  const int pg0 = s0 / kPage;
+  const int npg = (s1 - s0 + kPage - 1) / kPage;
+  const bool bt_cached = kIds && npg <= kCBtCache;
+  if (bt_cached)
+    for (int i = tid; i < npg; i += NT) s.bt[i] = bt_row[pg0 + i];
+
+  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistBins;
+  if (leader) {
+    // Digit 1 from the scoring kernel's histogram (cleared below once used):
+    // coalesced loads, staged so that each thread owns consecutive bins; the
+    // result goes to every CTA of the cluster.
+    {
+      const uint4* g4 = reinterpret_cast<const uint4*>(g_hist);
+      uint4 x[kHistPer / 4];
+#pragma unroll
+      for (int q = 0; q < kHistPer / 4; ++q) x[q] = g4[q * NT + tid];
+#pragma unroll
+      for (int q = 0; q < kHistPer / 4; ++q) s.u.hist1[q * NT + tid] = x[q];
+    }
+    __syncthreads();
+    uint32_t h[kHistPer];
+#pragma unroll
+    for (int q = 0; q < kHistPer / 4; ++q) {
+      const uint4 x = s.u.hist1[tid * (kHistPer / 4) + q];
+      h[4 * q] = x.x; h[4 * q + 1] = x.y; h[4 * q + 2] = x.z; h[4 * q + 3] = x.w;
+    }
+    find_threshold<NT, kHistPer>(s.sc, h, kTopK);  // its barriers free the staging area
+    wait();
+    if (tid < C) {
+      int* dst = sm100::cluster_map(s.bcast, static_cast<uint32_t>(tid));
+      dst[0] = s.sc.sel_bin;
+      dst[1] = s.sc.sel_above;
+      dst[2] = s.sc.sel_count;
+    }
+    uint4* g4 = reinterpret_cast<uint4*>(g_hist);
+#pragma unroll
+    for (int q = 0; q < kHistPer / 4; ++q) g4[q * NT + tid] = make_uint4(0u, 0u, 0u, 0u);
+  } else {
+    wait();
+  }
+  // The first digit and the leader's counters are ready for the cluster.
+  arrive(true);
+  wait();
+  const uint32_t bin1 = static_cast<uint32_t>(s.bcast[0]);
+  const int above1 = s.bcast[1];
+  const int n1 = s.bcast[2];
+  const bool use_cand = n1 <= kCap * C;
+  const uint32_t key_lo = bin1 << (32 - kHistBits);                 // first key of the pivot bin
+  const uint32_t key_top = key_lo | ((1u << (32 - kHistBits)) - 1u);  // last key of the pivot bin
+  int* lead_out = sm100::cluster_map(&s.out_count, 0u);
+  int* lead_overflow = sm100::cluster_map(&s.overflow, 0u);
+
+  auto value_of = [&](int i) -> int32_t {
+    if constexpr (kIds) {
+      const int32_t page = bt_cached ? s.bt[(i >> 6) - pg0] : bt_row[i >> 6];
+      return page * kPage + (i & (kPage - 1));
+    } else {
+      return i;
+    }
+  };
+
+  for (int base = s0; base < s1; base += kRound) {
+    if (base != s0) load_round(base);
+    sm100::cp_async_wait_all();  // this thread's own pieces have landed
+    // Bit e of gtm / inm: entry e of this thread is above / in-or-above the
+    // pivot bin.  Groups of 4 entries wholly past s1 are skipped (uniformly
+    // across the block: the groups are NT*4 entries apart).
+    uint32_t gtm = 0u, inm = 0u;
+    const int groups = min(kCPer / 4, (s1 - base + 4 * NT - 1) / (4 * NT));
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) {
+      if (u < groups) {
+        const uint4 w = *reinterpret_cast<const uint4*>(&s.vals[u][tid]);
+        const uint32_t k4[4] = {key_of_bits(w.x), key_of_bits(w.y), key_of_bits(w.z), key_of_bits(w.w)};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (k4[c] > key_top) gtm |= 1u << (4 * u + c);
+          if (k4[c] >= key_lo) inm |= 1u << (4 * u + c);
+        }
+      }
+    }
+    if (base + kRound > s1) {  // the segment's last round: drop entries at or past s1
+      uint32_t valid = 0u;
+#pragma unroll
+      for (int u = 0; u < kCPer / 4; ++u) {
+        const int i0 = base + 4 * (u * NT + tid);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (i0 + c < s1) valid |= 1u << (4 * u + c);
+      }
+      gtm &= valid;
+      inm &= valid;
+    }
+    const uint32_t eqm = use_cand ? (inm & ~gtm) : 0u;
+    uint32_t tot;
+    const uint32_t pre = block_scan_packed<NT>(s.sc, __popc(gtm) | (__popc(eqm) << 16), &tot);
+    const int n_gt = static_cast<int>(tot & 0xFFFFu), n_eq = static_cast<int>(tot >> 16);
+    if (tid == 0) s.base_out = n_gt ? atomicAdd(lead_out, n_gt) : 0;
+    __syncthreads();
+    int pos = s.base_out + static_cast<int>(pre & 0xFFFFu);
+    int cpos = s.cand_count + static_cast<int>(pre >> 16);
+    uint32_t m = gtm | eqm;
+    while (m) {
+      const int e = __ffs(m) - 1;
+      m &= m - 1u;
+      const float x = reinterpret_cast<const float*>(&s.vals[e >> 2][tid])[e & 3];
+      const uint32_t key = key_of_bits(__float_as_uint(x));
+      const int32_t val = value_of(base + 4 * ((e >> 2) * NT + tid) + (e & 3));
+      if ((gtm >> e) & 1u) {
+        out.emit(pos++, val, key);
+      } else {
+        if (cpos < kCap) {
+          s.u.cand.key[cpos] = key;
+          s.u.cand.val[cpos] = val;
+        } else {
+          atomicOr(lead_overflow, 1);
+        }
+        ++cpos;
+        atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
+      }
+    }
+    __syncthreads();  // base_out, cand_count and the scan scratch are reused
+    if (tid == 0) s.cand_count += n_eq;
+  }
+  // Every CTA's candidates, histogram and output slots are final.
+  arrive(true);
+  wait();
+
+  if (leader) {
+    // Counts, list addresses and the summed second-digit histogram of every
+    // CTA of the cluster.
+    if (tid < 32) {
+      int cnt = 0;
+      if (tid < C) {
+        const uint32_t q = static_cast<uint32_t>(tid);
+        cnt = min(*sm100::cluster_map(&s.cand_count, q), kCap);
+        s.cand_key_of[tid] = sm100::cluster_map(s.u.cand.key, q);
+        s.cand_val_of[tid] = sm100::cluster_map(s.u.cand.val, q);
+      }
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (tid >= off) incl += y;
+      }
+      if (tid < C) s.gather_base[tid] = incl - cnt;
+      if (tid == C - 1) s.gather_base[C] = incl;
+    }
+    uint32_t h2[kB2Per];
+#pragma unroll
+    for (int i = 0; i < kB2Per; ++i) h2[i] = 0u;
+#pragma unroll
+    for (int q = 0; q < kMaxCluster; ++q) {
+      if (q < C) {
+        const uint32_t* src = sm100::cluster_map(&s.hist[tid * kB2Per], static_cast<uint32_t>(q));
+        if constexpr (kB2Per == 4) {
+          const uint4 x = *reinterpret_cast<const uint4*>(src);
+          h2[0] += x.x; h2[1] += x.y; h2[2] += x.z; h2[3] += x.w;
+        } else {
+#pragma unroll
+          for (int i = 0; i < kB2Per; ++i) h2[i] += src[i];
+        }
+      }
+    }
+    __syncthreads();  // gather_base, list addresses; every thread has read its own bins
+
+    const bool listed = use_cand && s.overflow == 0;
+    const int k1 = kTopK - above1;
+    if (!listed) {
+      // The pivot bin's keys were not all kept: second digit over the row in
+      // global memory instead.
+      for (int i = tid; i < kBins2; i += NT) s.hist[i] = 0u;
+      __syncthreads();
+      for (int base = 0; base < L; base += NT) {
+        const int i = base + tid;
+        const uint32_t key = i < L ? ordered_key(row[i]) : 0u;
+        hist_add(s.hist, (key >> 10) & (kBins2 - 1), i < L && (key >> (32 - kHistBits)) == bin1);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int i = 0; i < kB2Per; ++i) h2[i] = s.hist[tid * kB2Per + i];
+    }
+    find_threshold<NT, kB2Per>(s.sc, h2, k1);
+    const uint32_t prefix2 = (bin1 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+    const int k2 = k1 - s.sc.sel_above;
+
+    // Entry j of the pivot bin: from the cluster's lists, or the row.
+    const int n3 = listed ? s.gather_base[C] : L;
+    auto key_at = [&](int j, int* q_out) -> uint32_t {
+      if (!listed) return ordered_key(row[j]);
+      int q = 0;
+      while (q + 1 < C && j >= s.gather_base[q + 1]) ++q;
+      *q_out = q;
+      return s.cand_key_of[q][j - s.gather_base[q]];
+    };
+
+    // Third digit over the entries that share the 22-bit prefix.
+    for (int i = tid; i < kBins2; i += NT) s.hist[i] = 0u;
+    __syncthreads();
+    for (int base = 0; base < n3; base += NT) {
+      const int j = base + tid;
+      int q = 0;
+      const uint32_t key = j < n3 ? key_at(j, &q) : 0u;
+      hist_add(s.hist, key & (kBins2 - 1), j < n3 && (key >> 10) == prefix2);
+    }
+    __syncthreads();
+    uint32_t h3[kB2Per];
+#pragma unroll
+    for (int i = 0; i < kB2Per; ++i) h3[i] = s.hist[tid * kB2Per + i];
+    find_threshold<NT, kB2Per>(s.sc, h3, k2);
+    const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+    const int k3 = k2 - s.sc.sel_above;  // how many keys equal to the pivot are taken
+
+    // Emit the pivot bin's keys above the pivot, and k3 keys equal to it.
+    for (int base = 0; base < n3; base += NT) {
+      const int j = base + tid;
+      int q = 0;
+      const uint32_t key = j < n3 ? key_at(j, &q) : 0u;
+      const bool in_bin = j < n3 && (key >> (32 - kHistBits)) == bin1;
+      const bool gt = in_bin && key > pivot;
+      const bool eq = in_bin && key == pivot;
+      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+      const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+      if (gt || (eq && ticket < k3)) {
+        int32_t val;
+        if (listed) {
+          val = s.cand_val_of[q][j - s.gather_base[q]];
+        } else if constexpr (kIds) {
+          val = physical_id(bt_row, j);
+        } else {
+          val = j;
+        }
+        out.emit(gt ? pos : kTopK - k3 + ticket, val, key);
+      }
+    }
+  }
+  // The leader has finished reading the other CTAs' shared memory.
+  if (C > 1) {
+    sm100::cluster_arrive_release();
+    sm100::cluster_wait_acquire();
+  }
+}
+
+// ------------------------------------------------------------ one CTA per row
+
+constexpr int kWThreads = 1024;
+constexpr int kWRound = kWThreads * kCPer;  // 32768 entries per round
+constexpr int kWCap = 8192;                 // pivot-bin keys kept
+constexpr int kWBtCache = 2048;             // block-table entries of a row in smem (131072 tokens)
+constexpr int kSmall = 64;                  // second-digit bin small enough for one warp to rank
+
+struct WideSmem {
+  float4 vals[kCPer / 4][kWThreads];  // the current round's logits
+  uint32_t cand_key[kWCap];           // keys in the pivot bin and their output
+  int32_t cand_val[kWCap];            // values (physical id or token)
+  uint32_t hist[kBins2];              // second (then third) digit histogram
+  int32_t bt[kWBtCache];              // the row's pages
+  uint32_t small_key[kSmall];         // keys of the second-digit bin
+  int32_t small_val[kSmall];
+  Scan sc;
+  int out_count;
+  int cand_count;
+  int small_count;
+  int eq_count;
+};
+
+constexpr int kWideSmemBytes = static_cast<int>(sizeof(WideSmem));
+static_assert(kWideSmemBytes <= 232448, "the wide CTA must fit");
+static_assert(kBins2 == kWThreads && kHistBins == 4 * kWThreads, "bin ownership");
+
+// One 1024-thread CTA per row: no cross-CTA traffic, and no block-wide scan
+// in the pass (output and candidate slots come from one shared atomic per
+// warp).  After the pass, the second digit is found from the histogram the
+// pass built; the few keys sharing the 22-bit prefix (at most 64, else a
+// third digit is counted) are ranked by one warp.
+template <bool kIds>
+__global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectLaunch p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  WideSmem& s = *reinterpret_cast<WideSmem*>(smem_raw);
+  grid_dep_wait();
+  grid_dep_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31;
   const int b = blockIdx.x;
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
   const float* row = p.logits + static_cast<size_t>(b) * p.ld;
-  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistBins;
+  RowOut<kIds> out;
+  out.ids = kIds ? p.out_ids + static_cast<size_t>(b) * kTopK : nullptr;
+  out.scores = kIds ? nullptr : p.out_scores + static_cast<size_t>(b) * kTopK;
+  out.tokens = kIds ? nullptr : p.out_tokens + static_cast<size_t>(b) * kTopK;
+  out.offset = p.token_offset;
 
-  if (p.out_ids) {
-    int32_t* out = p.out_ids + static_cast<size_t>(b) * kTopK;
-    if (L <= kTopK) {
-      for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
-      return;
-    }
-    // The row's block table in shared memory: emitting an id then costs no
-    // dependent global load.
-    const int npages = (L + kPage - 1) / kPage;
-    const int32_t* bt_ids = bt_row;
-    if (npages <= kBtCache) {
-      for (int i = threadIdx.x; i < npages; i += kThreads) s.bt[i] = bt_row[i];
-      bt_ids = s.bt;  // made visible by the barrier inside select_topk
-    }
-    select_topk<true>(RowSrc{row}, row, IdsOut{out, bt_ids}, L, g_hist, s);
-  } else {
-    float* sc = p.out_scores + static_cast<size_t>(b) * kTopK;
-    int32_t* tk = p.out_tokens + static_cast<size_t>(b) * kTopK;
-    if (L <= kTopK) {
-      for (int i = threadIdx.x; i < kTopK; i += kThreads) {
-        sc[i] = i < L ? row[i] : -INFINITY;
-        tk[i] = i < L ? i + p.token_offset : -1;
+  if (L <= kTopK) {  // every token is selected
+    for (int i = tid; i < kTopK; i += kWThreads) {
+      if constexpr (kIds) {
+        out.ids[i] = i < L ? physical_id(bt_row, i) : -1;
+      } else {
+        out.scores[i] = i < L ? row[i] : -INFINITY;
+        out.tokens[i] = i < L ? i + p.token_offset : -1;
       }
-      return;
     }
-    select_topk<true>(RowSrc{row}, row, PairsOut{sc, tk, p.token_offset}, L, g_hist, s);
+    return;
+  }
+
+  // First round of logits into shared memory (each thread copies, and later
+  // reads, its own 16-B pieces; the row buffer is padded to 64 entries).
+  const float4* row4 = reinterpret_cast<const float4*>(row);
+  auto load_round = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) {
+      const int j = base / 4 + u * kWThreads + tid;
+      if (4 * j < L) sm100::cp_async_16(&s.vals[u][tid], row4 + j, 16u);
+    }
+  };
+  load_round(0);
+  const int npg = (L + kPage - 1) / kPage;
+  const bool bt_cached = kIds && npg <= kWBtCache;
+  if (bt_cached)
+    for (int i = tid; i < npg; i += kWThreads) s.bt[i] = bt_row[i];
+  s.hist[tid] = 0u;
+  if (tid == 0) {
+    s.out_count = 0;
+    s.cand_count = 0;
+    s.small_count = 0;
+    s.eq_count = 0;
+  }
+
+  // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
+  // histogram (one coalesced 16-B load), cleared for the next call once read.
+  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
+  uint32_t h1[4];
+  {
+    const uint4 x = g4[tid];
+    h1[0] = x.x; h1[1] = x.y; h1[2] = x.z; h1[3] = x.w;
+  }
+  find_threshold<kWThreads, 4>(s.sc, h1, kTopK);  // its barriers publish the zeroed counters
+  g4[tid] = make_uint4(0u, 0u, 0u, 0u);
+  const uint32_t bin1 = static_cast<uint32_t>(s.sc.sel_bin);
+  const int above1 = s.sc.sel_above;
+  const int n1 = s.sc.sel_count;
+  const bool listed = n1 <= kWCap;
+  const uint32_t key_lo = bin1 << (32 - kHistBits);
+  const uint32_t key_top = key_lo | ((1u << (32 - kHistBits)) - 1u);
+  const int k1 = kTopK - above1;
+
+  auto value_of = [&](int i) -> int32_t {
+    if constexpr (kIds) {
+      const int32_t page = bt_cached ? s.bt[i >> 6] : bt_row[i >> 6];
+      return page * kPage + (i & (kPage - 1));
+    } else {
+      return i;
+    }
+  };
+
+  for (int base = 0; base < L; base += kWRound) {
+    if (base != 0) load_round(base);
+    sm100::cp_async_wait_all();  // this thread's own pieces have landed
+    uint32_t gtm = 0u, inm = 0u;
+    const int groups = min(kCPer / 4, (L - base + 4 * kWThreads - 1) / (4 * kWThreads));
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) {
+      if (u < groups) {
+        const uint4 w = *reinterpret_cast<const uint4*>(&s.vals[u][tid]);
+        const uint32_t k4[4] = {key_of_bits(w.x), key_of_bits(w.y), key_of_bits(w.z), key_of_bits(w.w)};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (k4[c] > key_top) gtm |= 1u << (4 * u + c);
+          if (k4[c] >= key_lo) inm |= 1u << (4 * u + c);
+        }
+      }
+    }
+    if (base + kWRound > L) {  // the last round: drop entries at or past L
+      uint32_t valid = 0u;
+#pragma unroll
+      for (int u = 0; u < kCPer / 4; ++u) {
+        const int i0 = base + 4 * (u * kWThreads + tid);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (i0 + c < L) valid |= 1u << (4 * u + c);
+      }
+      gtm &= valid;
+      inm &= valid;
+    }
+    const uint32_t eqm = listed ? (inm & ~gtm) : 0u;
+    int pos = warp_alloc_n(&s.out_count, __popc(gtm));
+    int cpos = warp_alloc_n(&s.cand_count, __popc(eqm));
+    uint32_t m = gtm | eqm;
+    while (m) {
+      const int e = __ffs(m) - 1;
+      m &= m - 1u;
+      const float x = reinterpret_cast<const float*>(&s.vals[e >> 2][tid])[e & 3];
+      const uint32_t key = key_of_bits(__float_as_uint(x));
+      const int32_t val = value_of(base + 4 * ((e >> 2) * kWThreads + tid) + (e & 3));
+      if ((gtm >> e) & 1u) {
+        out.emit(pos++, val, key);
+      } else {
+        s.cand_key[cpos] = key;  // cpos < n1 <= kWCap
+        s.cand_val[cpos] = val;
+        ++cpos;
+        atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
+      }
+    }
+  }
+  __syncthreads();  // candidates, second-digit counts and output slots are final
+
+  if (!listed) {
+    // More keys in the pivot bin than the list holds: the second digit over
+    // the row in global memory.
+    for (int base = 0; base < L; base += kWThreads) {
+      const int i = base + tid;
+      const uint32_t key = i < L ? ordered_key(row[i]) : 0u;
+      hist_add(s.hist, (key >> 10) & (kBins2 - 1), i < L && (key >> (32 - kHistBits)) == bin1);
+    }
+    __syncthreads();
+  }
+  uint32_t h2[1] = {s.hist[tid]};
+  find_threshold<kWThreads, 1>(s.sc, h2, k1);
+  const uint32_t prefix2 = (bin1 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k2 = k1 - s.sc.sel_above;  // keys still needed from the second-digit bin
+  const int n2 = s.sc.sel_count;
+  const bool small = n2 <= kSmall;
+
+  // The pivot bin's entries: the list, or the row.
+  const int n3 = listed ? n1 : L;
+  auto key_at = [&](int j) -> uint32_t {
+    if (listed) return s.cand_key[j];
+    const uint32_t key = ordered_key(row[j]);
+    return (key >> (32 - kHistBits)) == bin1 ? key : 0u;
+  };
+  auto val_at = [&](int j) -> int32_t {
+    if (listed) return s.cand_val[j];
+    if constexpr (kIds) return physical_id(bt_row, j); else return j;
+  };
+
+  if (small) {
+    // Emit the keys above the 22-bit prefix; collect the prefix's keys.
+    for (int base = 0; base < n3; base += kWThreads) {
+      const int j = base + tid;
+      const uint32_t key = j < n3 ? key_at(j) : 0u;
+      const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+      const bool gt = in && (key >> 10) > prefix2;
+      const bool eq = in && (key >> 10) == prefix2;
+      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+      const int q = warp_alloc_n(&s.small_count, eq ? 1 : 0);
+      if (gt) out.emit(pos, val_at(j), key);
+      if (eq && q < kSmall) {
+        s.small_key[q] = key;
+        s.small_val[q] = val_at(j);
+      }
+    }
+    __syncthreads();
+    if (tid < 32) {
+      // Rank the n2 keys (largest first, ties by list position); the k2 best
+      // take the last k2 slots.
+      const int n = min(s.small_count, kSmall);
+      const uint32_t ka = lane < n ? s.small_key[lane] : 0u;
+      const uint32_t kb = lane + 32 < n ? s.small_key[lane + 32] : 0u;
+      int ra = 0, rb = 0;
+      for (int o = 0; o < 32; ++o) {
+        const uint32_t xa = __shfl_sync(0xffffffffu, ka, o);
+        const uint32_t xb = __shfl_sync(0xffffffffu, kb, o);
+        if (o < n) {
+          ra += (xa > ka || (xa == ka && o < lane)) ? 1 : 0;
+          rb += (xa > kb || (xa == kb && o < lane + 32)) ? 1 : 0;
+        }
+        if (o + 32 < n) {
+          ra += (xb > ka || (xb == ka && o + 32 < lane)) ? 1 : 0;
+          rb += (xb > kb || (xb == kb && o < lane)) ? 1 : 0;
+        }
+      }
+      if (lane < n && ra < k2) out.emit(kTopK - k2 + ra, s.small_val[lane], ka);
+      if (lane + 32 < n && rb < k2) out.emit(kTopK - k2 + rb, s.small_val[lane + 32], kb);
+    }
+    return;
+  }
+
+  // Many keys share the 22-bit prefix: count the third digit over them.
+  s.hist[tid] = 0u;
+  __syncthreads();
+  for (int base = 0; base < n3; base += kWThreads) {
+    const int j = base + tid;
+    const uint32_t key = j < n3 ? key_at(j) : 0u;
+    hist_add(s.hist, key & (kBins2 - 1), j < n3 && key != 0u && (key >> 10) == prefix2);
+  }
+  __syncthreads();
+  uint32_t h3[1] = {s.hist[tid]};
+  find_threshold<kWThreads, 1>(s.sc, h3, k2);
+  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k3 = k2 - s.sc.sel_above;  // how many keys equal to the pivot are taken
+  for (int base = 0; base < n3; base += kWThreads) {
+    const int j = base + tid;
+    const uint32_t key = j < n3 ? key_at(j) : 0u;
+    const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+    const bool gt = in && key > pivot;
+    const bool eq = in && key == pivot;
+    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    if (gt) out.emit(pos, val_at(j), key);
+    if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    merge_kernel(const float* scores, const int32_t* tokens, int n_cand, const int32_t* bt_row,
+// ------------------------------------------------------------ merge
+
+constexpr int kMThreads = 512;
+
+struct MergeSmem {
+  uint32_t hist[kHistBins];
+  uint32_t cand_key[kCandCap];
+  int32_t cand_idx[kCandCap];
+  Scan sc;
+  int out_count;
+  int cand_count;
+  int eq_count;
+};
+
+constexpr int kMergeSmemBytes = static_cast<int>(sizeof(MergeSmem));
+
+// Key of candidate i of a (score, token) list; padding (token -1) and tokens
+// >= L are no entry (key 0, never produced for a real logit: it is the image
+// of one NaN bit pattern only).
+__device__ __forceinline__ uint32_t cand_key_of(const float* scores, const int32_t* tokens, int L, int i) {
+  const int t = tokens[i];
+  return (t >= 0 && t < L) ? ordered_key(scores[i]) : 0u;
+}
+
+__global__ void __launch_bounds__(kMThreads, 1)
+    merge_kernel(const float* scores, const int32_t* tokens, int n, const int32_t* bt_row,
                  int max_pages, const int32_t* seq_len, int32_t* out) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  SelSmem& s = *reinterpret_cast<SelSmem*>(smem_raw);
+  MergeSmem& s = *reinterpret_cast<MergeSmem*>(smem_raw);
+  const int tid = threadIdx.x;
   const int L = row_len(seq_len, 0, max_pages, nullptr);
   if (L <= kTopK) {
-    for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
+    for (int i = tid; i < kTopK; i += kMThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
     return;
   }
-  // Slots stay -1 if the candidates hold fewer than kTopK real entries.
-  for (int i = threadIdx.x; i < kTopK; i += kThreads) out[i] = -1;
+  // Slots stay -1 if the lists hold fewer than kTopK real entries.
+  for (int i = tid; i < kTopK; i += kMThreads) out[i] = -1;
+  for (int i = tid; i < kHistBins; i += kMThreads) s.hist[i] = 0u;
+  if (tid == 0) {
+    s.out_count = 0;
+    s.cand_count = 0;
+    s.eq_count = 0;
+  }
   __syncthreads();
-  select_topk<false>(CandSrc{scores, tokens, L}, nullptr, MergeOut{out, bt_row, tokens}, n_cand,
-                     nullptr, s);
+  for (int base = 0; base < n; base += kMThreads) {
+    const int i = base + tid;
+    const uint32_t key = i < n ? cand_key_of(scores, tokens, L, i) : 0u;
+    hist_add(s.hist, key >> (32 - kHistBits), key != 0u);
+  }
+  __syncthreads();
+  constexpr int kPer1 = kHistBins / kMThreads, kPer2 = kBins2 / kMThreads;
+  uint32_t h1[kPer1];
+#pragma unroll
+  for (int i = 0; i < kPer1; ++i) h1[i] = s.hist[tid * kPer1 + i];
+  find_threshold<kMThreads, kPer1>(s.sc, h1, kTopK);
+  const uint32_t bin1 = static_cast<uint32_t>(s.sc.sel_bin);
+  const int k1 = kTopK - s.sc.sel_above;
+  const bool use_cand = s.sc.sel_count <= kCandCap;
+
+  // Emit keys above the pivot bin; collect the pivot bin.
+  for (int base = 0; base < n; base += kMThreads) {
+    const int i = base + tid;
+    const uint32_t key = i < n ? cand_key_of(scores, tokens, L, i) : 0u;
+    const uint32_t bb = key >> (32 - kHistBits);
+    const bool gt = key != 0u && bb > bin1;
+    const bool eq = use_cand && key != 0u && bb == bin1;
+    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    if (gt) out[pos] = physical_id(bt_row, tokens[i]);
+    const int cpos = warp_alloc_n(&s.cand_count, eq ? 1 : 0);
+    if (eq) {
+      s.cand_key[cpos] = key;
+      s.cand_idx[cpos] = i;
+    }
+  }
+  __syncthreads();
+  const int m = use_cand ? s.cand_count : n;
+  auto bucket = [&](int j) -> uint32_t {  // key of the j-th pivot-bin entry, or 0
+    if (j >= m) return 0u;
+    if (use_cand) return s.cand_key[j];
+    const uint32_t key = cand_key_of(scores, tokens, L, j);
+    return (key >> (32 - kHistBits)) == bin1 ? key : 0u;
+  };
+  auto index_of = [&](int j) { return use_cand ? s.cand_idx[j] : j; };
+
+  for (int i = tid; i < kBins2; i += kMThreads) s.hist[i] = 0u;
+  __syncthreads();
+  for (int base = 0; base < m; base += kMThreads) {
+    const uint32_t key = bucket(base + tid);
+    hist_add(s.hist, (key >> 10) & (kBins2 - 1), key != 0u);
+  }
+  __syncthreads();
+  uint32_t h2[kPer2];
+#pragma unroll
+  for (int i = 0; i < kPer2; ++i) h2[i] = s.hist[tid * kPer2 + i];
+  find_threshold<kMThreads, kPer2>(s.sc, h2, k1);
+  const uint32_t prefix2 = (bin1 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k2 = k1 - s.sc.sel_above;
+
+  for (int i = tid; i < kBins2; i += kMThreads) s.hist[i] = 0u;
+  __syncthreads();
+  for (int base = 0; base < m; base += kMThreads) {
+    const uint32_t key = bucket(base + tid);
+    hist_add(s.hist, key & (kBins2 - 1), key != 0u && (key >> 10) == prefix2);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kPer2; ++i) h2[i] = s.hist[tid * kPer2 + i];
+  find_threshold<kMThreads, kPer2>(s.sc, h2, k2);
+  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k3 = k2 - s.sc.sel_above;
+
+  for (int base = 0; base < m; base += kMThreads) {
+    const int j = base + tid;
+    const uint32_t key = bucket(j);
+    const bool gt = key != 0u && key > pivot;
+    const bool eq = key != 0u && key == pivot;
+    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    if (gt) out[pos] = physical_id(bt_row, tokens[index_of(j)]);
+    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    if (eq && ticket < k3) out[kTopK - k3 + ticket] = physical_id(bt_row, tokens[index_of(j)]);
+  }
 }
 
 // Rows that all fit in the top-K (max_pages * 64 <= 2048): the output is the
@@ -497,9 +1004,19 @@ cudaError_t ensure_attrs() {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64 && g_attr_done[dev]) return cudaSuccess;
-  e = cudaFuncSetAttribute(select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  e = cudaFuncSetAttribute(select_rows_kernel<true, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           row_smem_bytes<256>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_rows_kernel<false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             row_smem_bytes<256>());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_wide_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kWideSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_wide_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kWideSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmemBytes);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64) g_attr_done[dev] = true;
   return cudaSuccess;
@@ -507,23 +1024,63 @@ cudaError_t ensure_attrs() {
 
 }  // namespace
 
-int select_smem_bytes() { return kSmemBytes; }
+int select_smem_bytes() { return kWideSmemBytes; }
+
+SelectShape select_shape(int rows, int max_pages, int sms) {
+  SelectShape sh;
+#if defined(DSAI_SELECT_FORCE_CLUSTER)
+  const bool wide = false;
+#elif defined(DSAI_SELECT_FORCE_WIDE)
+  const bool wide = true;
+#else
+  // One wide CTA per row once the rows alone occupy a good share of the SMs.
+  const bool wide = static_cast<long long>(rows) * 4 >= static_cast<long long>(sms);
+#endif
+  if (wide) {
+    sh.threads = kWThreads;
+    sh.cluster = 1;
+    return sh;
+  }
+  // As many CTAs per row as keep every CTA of the launch resident at once (at
+  // most 8, a portable cluster), but no more than one per 1024 entries of the
+  // longest possible row.
+  const long long max_len = static_cast<long long>(max_pages) * kPage;
+  const long long resident = static_cast<long long>(sms) * SelShape<256>::kCtasPerSm;
+  long long c = rows > 0 ? resident / rows : 1;
+  const long long useful = (max_len + 1023) / 1024;
+  if (c > useful) c = useful;
+  if (c > kMaxCluster) c = kMaxCluster;
+  if (c < 1) c = 1;
+  sh.threads = 256;
+  sh.cluster = static_cast<int>(c);
+  return sh;
+}
 
 cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
   cudaError_t e = ensure_attrs();
   if (e != cudaSuccess) return e;
   if (p.rows <= 0) return cudaSuccess;
+  const SelectShape sh = select_shape(p.rows, p.max_pages, p.sms);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.rows);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * static_cast<unsigned>(sh.cluster));
+  cfg.blockDim = dim3(static_cast<unsigned>(sh.threads));
+  cfg.dynamicSmemBytes = sh.threads == kWThreads ? kWideSmemBytes : row_smem_bytes<256>();
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(sh.cluster);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, select_kernel, p);
+  cfg.numAttrs = sh.cluster > 1 ? 2 : 1;
+  if (sh.threads == kWThreads) {
+    if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_wide_kernel<true>, p);
+    return cudaLaunchKernelEx(&cfg, select_wide_kernel<false>, p);
+  }
+  if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_rows_kernel<true, 256>, p);
+  return cudaLaunchKernelEx(&cfg, select_rows_kernel<false, 256>, p);
 }
 
 cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,
@@ -543,8 +1100,8 @@ cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
                          int32_t* out, cudaStream_t stream) {
   cudaError_t e = ensure_attrs();
   if (e != cudaSuccess) return e;
-  merge_kernel<<<1, kThreads, kSmemBytes, stream>>>(scores, tokens, n_cand, bt_row, max_pages,
-                                                    seq_len, out);
+  merge_kernel<<<1, kMThreads, kMergeSmemBytes, stream>>>(scores, tokens, n_cand, bt_row, max_pages,
+                                                          seq_len, out);
   return cudaGetLastError();
 }
 

@@ -83,6 +83,56 @@ __device__ __forceinline__ void grid_dep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- clusters
+// Rank of this CTA in its cluster, the cluster's size, and the cluster's
+// index in the grid (x).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+
+// Split cluster barrier: every thread of every CTA of the cluster arrives
+// (release: its earlier writes, shared or global, become visible to the
+// cluster) and later waits (acquire).  Like __syncthreads, every thread must
+// take the same number of arrive/wait pairs on every path.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+// Arrive without ordering any memory: used at kernel start so that a later
+// wait guarantees every CTA of the cluster is running (its shared memory may
+// then be accessed).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Generic address of the variable at `p` (this CTA's shared memory) in the
+// shared memory of cluster CTA `rank`; ordinary loads, stores and atomics
+// through it access that CTA's shared memory.
+template <class T>
+__device__ __forceinline__ T* cluster_map(T* p, uint32_t rank) {
+  uint64_t out;
+  asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+  return reinterpret_cast<T*>(out);
+}
+
 // ---------------------------------------------------------------- TMA
 // 3-D tiled tensor load into shared memory, completion counted in bytes on
 // `bar`.  The tensor map lives in kernel parameter space (__grid_constant__).

@@ -123,6 +123,39 @@ def test_ties_all_equal_logits(oracle_mod):
     assert np.all(glog[0, :5000] == 0)
 
 
+def test_ties_overflow_candidate_lists(oracle_mod):
+    """One long row of equal logits: every CTA of the row's cluster finds
+    more pivot-bin keys than its list holds, so the selection falls back to
+    refining over the row in global memory."""
+    inp = W.make_inputs([40000], seed=27)
+    inp.q = torch.zeros_like(inp.q)
+    ids, glog, status = gpu_run(inp)
+    assert status == 0
+    check(oracle_mod, inp, ids, glog)
+    assert np.all(glog[0, :40000] == 0)
+
+
+def test_one_cta_per_row_paths(oracle_mod):
+    """A batch large enough for one selection CTA per row, mixing the
+    refinement paths: an all-equal row longer than the pivot list (refine
+    over the row), an all-equal row that fits it (third digit over the list),
+    64-token groups of equal logits, rows at the 2048 boundary, and ordinary
+    rows (second digit, then one warp ranks the last keys)."""
+    rng = np.random.default_rng(28)
+    lens = [20000, 5000, 30000, 2048, 2049] + rng.integers(3000, 12000, 35).tolist()
+    inp = W.make_inputs(lens, seed=28)
+    inp.q[0].zero_()
+    inp.q[1].zero_()
+    bt2 = inp.block_table[2, : (30000 + 63) // 64].long()
+    flat = inp.k_cache.view(-1, 8448)
+    flat[bt2, 128:8192] = flat[bt2, 0:128].repeat(1, 63)
+    flat[bt2, 8192 + 4:8448] = flat[bt2, 8192:8196].repeat(1, 63)
+    ids, glog, status = gpu_run(inp)
+    assert status == 0
+    check(oracle_mod, inp, ids, glog)
+    assert np.all(glog[0, :20000] == 0) and np.all(glog[1, :5000] == 0)
+
+
 def test_many_ties_in_pivot_bucket(oracle_mod):
     """Quantised logits with heavy ties around the boundary (the pivot bin
     overflows the candidate list and the refinement re-reads the row)."""

@@ -25,10 +25,11 @@
 //               stage is released as soon as its MMAs complete.
 //   warps 2-5   epilogue: tcgen05.ld of the 128x64 fp32 tile (one token per
 //               thread, 64 head scores in registers), ReLU, head weights,
-//               token scale, coalesced fp32 store, and one fire-and-forget
-//               reduction into the row's global histogram of 12-bit key
-//               prefixes (no group synchronisation, so a timed-out warp can
-//               never leave the others waiting).
+//               token scale, coalesced fp32 store, and fire-and-forget
+//               reductions into the row's global histogram of 12-bit key
+//               prefixes, one per distinct bin of the warp's 32 tokens (no
+//               group synchronisation beyond the warp, so a timed-out warp
+//               can never leave the others waiting).
 // Rows with L <= 2048 are skipped (their output does not depend on scores).
 #include "common.cuh"
 #include "launch.h"
@@ -366,7 +367,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
           hist_g = p.hist + static_cast<size_t>(cur_row) * kHistBins;
         }
-        if (!mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        // Waits are decided warp-wide: the warp runs warp-collective steps below.
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs))) {
+          fail(s, p.status);
+          break;
+        }
         tc_fence_after();
         uint32_t r0[32], r1[32];
         const uint32_t taddr = s.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -377,7 +382,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.tempty[acc]);
-        if (!mbar_wait(&s.sfull[sslot], sphase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.sfull[sslot], sphase, &s.abort, kWaitTimeoutNs))) {
+          fail(s, p.status);
+          break;
+        }
         const float sc = s.scale[sslot][tok];
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.sempty[sslot]);
@@ -398,9 +406,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         const float logit = ((a0 + a1) + (a2 + a3)) * sc;
         const int t_abs = c.j * kTileTok + tok;
-        if (t_abs < L) {
-          out_row[t_abs] = logit;
-          if (hist_row) atomicAdd(hist_g + (ordered_key(logit) >> (32 - kHistBits)), 1u);  // RED
+        const bool live = t_abs < L;
+        if (live) out_row[t_abs] = logit;
+        if (hist_row) {
+          // A row's logits crowd into few bins: lanes sharing a bin add once,
+          // so the row's reductions do not serialise on a few L2 addresses.
+          const uint32_t bin = ordered_key(logit) >> (32 - kHistBits);
+          const unsigned act = __ballot_sync(0xffffffffu, live);
+          if (live) {
+            const unsigned peers = __match_any_sync(act, bin);
+            if (lane == __ffs(peers) - 1) atomicAdd(hist_g + bin, static_cast<uint32_t>(__popc(peers)));  // RED
+          }
         }
         if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
         if (++sslot == kScaleSlots) { sslot = 0; sphase ^= 1u; }

@@ -232,8 +232,11 @@ struct RowOut {
   float* scores;
   int32_t* tokens;
   int32_t offset;
-  // val: the physical id (kIds) or the token index of the entry.
+  // val: the physical id (kIds) or the token index of the entry.  Slots
+  // outside the row are dropped: a histogram that disagrees with the logits
+  // (a corrupted workspace) can cost the result, never memory safety.
   __device__ __forceinline__ void emit(int pos, int32_t val, uint32_t key) const {
+    if (static_cast<unsigned>(pos) >= static_cast<unsigned>(kTopK)) return;
     if constexpr (kIds) {
       ids[pos] = val;
     } else {
@@ -600,6 +603,8 @@ struct WideSmem {
   int cand_count;
   int small_count;
   int eq_count;
+  int extreme[3];  // first-digit bins 0 and 4088..4095 (NaN, infinities) are not empty
+  uint64_t vbar[kCPer / 4];  // one bulk copy of 4 * kWThreads logits per barrier
 };
 
 constexpr int kWideSmemBytes = static_cast<int>(sizeof(WideSmem));
@@ -619,6 +624,11 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   grid_dep_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31;
   const int b = blockIdx.x;
+  // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
+  // histogram (one coalesced 16-B load, issued before the row length is
+  // known), cleared for the next call once read.
+  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
+  const uint4 hx = g4[tid];
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
   const float* row = p.logits + static_cast<size_t>(b) * p.ld;
@@ -640,17 +650,29 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     return;
   }
 
-  // First round of logits into shared memory (each thread copies, and later
-  // reads, its own 16-B pieces; the row buffer is padded to 64 entries).
-  const float4* row4 = reinterpret_cast<const float4*>(row);
+  // A round of logits into shared memory by thread 0: one bulk copy per
+  // group of 4 * kWThreads entries, each on its own barrier, so that the
+  // classification of a group starts as soon as it has landed.  Linear
+  // copies land in the [group][thread] float4 layout the threads read.  The
+  // row buffer is padded to 64 entries, so the copied size rounds up to 16 B
+  // inside it.
+  const uint64_t pol = sm100::l2_policy_evict_first();
   auto load_round = [&](int base) {
-#pragma unroll
-    for (int u = 0; u < kCPer / 4; ++u) {
-      const int j = base / 4 + u * kWThreads + tid;
-      if (4 * j < L) sm100::cp_async_16(&s.vals[u][tid], row4 + j, 16u);
+    const int n = min(L - base, kWRound);
+#pragma unroll 1
+    for (int u = 0; u * 4 * kWThreads < n; ++u) {
+      const int e0 = u * 4 * kWThreads;
+      const uint32_t bytes = static_cast<uint32_t>(((min(n - e0, 4 * kWThreads) + 3) / 4) * 16);
+      sm100::mbar_arrive_expect_tx(&s.vbar[u], bytes);
+      sm100::bulk_load(&s.vals[u][0], row + base + e0, bytes, &s.vbar[u], pol);
     }
   };
-  load_round(0);
+  if (tid == 0) {
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) sm100::mbar_init(&s.vbar[u], 1);
+    sm100::fence_mbar_init();
+    load_round(0);
+  }
   const int npg = (L + kPage - 1) / kPage;
   const bool bt_cached = kIds && npg <= kWBtCache;
   if (bt_cached)
@@ -663,14 +685,9 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     s.eq_count = 0;
   }
 
-  // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
-  // histogram (one coalesced 16-B load), cleared for the next call once read.
-  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
-  uint32_t h1[4];
-  {
-    const uint4 x = g4[tid];
-    h1[0] = x.x; h1[1] = x.y; h1[2] = x.z; h1[3] = x.w;
-  }
+  uint32_t h1[4] = {hx.x, hx.y, hx.z, hx.w};
+  if (tid == 0) s.extreme[0] = h1[0] != 0u;
+  if (tid >= kWThreads - 2) s.extreme[tid - (kWThreads - 3)] = (h1[0] | h1[1] | h1[2] | h1[3]) != 0u;
   find_threshold<kWThreads, 4>(s.sc, h1, kTopK);  // its barriers publish the zeroed counters
   g4[tid] = make_uint4(0u, 0u, 0u, 0u);
   const uint32_t bin1 = static_cast<uint32_t>(s.sc.sel_bin);
@@ -680,6 +697,13 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   const uint32_t key_lo = bin1 << (32 - kHistBits);
   const uint32_t key_top = key_lo | ((1u << (32 - kHistBits)) - 1u);
   const int k1 = kTopK - above1;
+  // A group of 4 logits whose float maximum is below the pivot bin's first
+  // value holds no key in or above the bin and is skipped after 4 compares.
+  // Exact for every non-NaN value (the key order is the float order, and a
+  // bound of +0.0 never skips -0.0); rows whose histogram shows NaNs or
+  // infinities (bins 0 and 4088..4095) classify every entry by its key.
+  const bool fast_skip = (s.extreme[0] | s.extreme[1] | s.extreme[2]) == 0;
+  const float f_lo = key_to_float(key_lo);
 
   auto value_of = [&](int i) -> int32_t {
     if constexpr (kIds) {
@@ -690,56 +714,76 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     }
   };
 
-  for (int base = 0; base < L; base += kWRound) {
-    if (base != 0) load_round(base);
-    sm100::cp_async_wait_all();  // this thread's own pieces have landed
+  bool copies_ok = true;
+  int round = 0;
+  for (int base = 0; base < L; base += kWRound, ++round) {
+    if (base != 0) {
+      __syncthreads();  // every thread is done with the previous round
+      if (tid == 0) load_round(base);
+    }
     uint32_t gtm = 0u, inm = 0u;
+    // Groups u < groups hold entries below L; only the last one can be
+    // partial (entries of group u end at base + 4 * (u + 1) * kWThreads).
     const int groups = min(kCPer / 4, (L - base + 4 * kWThreads - 1) / (4 * kWThreads));
 #pragma unroll
     for (int u = 0; u < kCPer / 4; ++u) {
       if (u < groups) {
-        const uint4 w = *reinterpret_cast<const uint4*>(&s.vals[u][tid]);
-        const uint32_t k4[4] = {key_of_bits(w.x), key_of_bits(w.y), key_of_bits(w.z), key_of_bits(w.w)};
+        if (!sm100::mbar_wait(&s.vbar[u], static_cast<uint32_t>(round & 1), nullptr, kWaitTimeoutNs)) {
+          copies_ok = false;  // classified from whatever landed; reported below
+        }
+        const float4 w = s.vals[u][tid];
+        if (fast_skip && fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) < f_lo) continue;
+        const uint32_t k4[4] = {key_of_bits(__float_as_uint(w.x)), key_of_bits(__float_as_uint(w.y)),
+                                key_of_bits(__float_as_uint(w.z)), key_of_bits(__float_as_uint(w.w))};
+        uint32_t g = 0u, n = 0u;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          if (k4[c] > key_top) gtm |= 1u << (4 * u + c);
-          if (k4[c] >= key_lo) inm |= 1u << (4 * u + c);
+          g |= static_cast<uint32_t>(k4[c] > key_top) << c;
+          n |= static_cast<uint32_t>(k4[c] >= key_lo) << c;
         }
+        if (u == groups - 1) {  // entries at or past L
+          const int left = L - (base + 4 * (u * kWThreads + tid));
+          const uint32_t valid = left >= 4 ? 0xFu : (left > 0 ? (1u << left) - 1u : 0u);
+          g &= valid;
+          n &= valid;
+        }
+        gtm |= g << (4 * u);
+        inm |= n << (4 * u);
       }
-    }
-    if (base + kWRound > L) {  // the last round: drop entries at or past L
-      uint32_t valid = 0u;
-#pragma unroll
-      for (int u = 0; u < kCPer / 4; ++u) {
-        const int i0 = base + 4 * (u * kWThreads + tid);
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (i0 + c < L) valid |= 1u << (4 * u + c);
-      }
-      gtm &= valid;
-      inm &= valid;
     }
     const uint32_t eqm = listed ? (inm & ~gtm) : 0u;
     int pos = warp_alloc_n(&s.out_count, __popc(gtm));
     int cpos = warp_alloc_n(&s.cand_count, __popc(eqm));
-    uint32_t m = gtm | eqm;
-    while (m) {
+    auto entry = [&](int e) { return base + 4 * ((e >> 2) * kWThreads + tid) + (e & 3); };
+    auto key_of_entry = [&](int e) {
+      return key_of_bits(__float_as_uint(reinterpret_cast<const float*>(&s.vals[e >> 2][tid])[e & 3]));
+    };
+    for (uint32_t m = gtm; m; m &= m - 1u) {  // above the pivot bin: straight to the output
       const int e = __ffs(m) - 1;
-      m &= m - 1u;
-      const float x = reinterpret_cast<const float*>(&s.vals[e >> 2][tid])[e & 3];
-      const uint32_t key = key_of_bits(__float_as_uint(x));
-      const int32_t val = value_of(base + 4 * ((e >> 2) * kWThreads + tid) + (e & 3));
-      if ((gtm >> e) & 1u) {
-        out.emit(pos++, val, key);
-      } else {
-        s.cand_key[cpos] = key;  // cpos < n1 <= kWCap
-        s.cand_val[cpos] = val;
-        ++cpos;
-        atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
+      out.emit(pos++, value_of(entry(e)), kIds ? 0u : key_of_entry(e));
+    }
+    for (uint32_t m = eqm; m; m &= m - 1u) {  // in the pivot bin: to the list
+      const int e = __ffs(m) - 1;
+      const uint32_t key = key_of_entry(e);
+      if (cpos < kWCap) {
+        s.cand_key[cpos] = key;
+        s.cand_val[cpos] = value_of(entry(e));
       }
+      ++cpos;
+      atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
     }
   }
   __syncthreads();  // candidates, second-digit counts and output slots are final
+  if (!copies_ok) {
+    report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+    // Never leave with a bulk copy in flight into this CTA's shared memory.
+    if (tid == 0) {
+      const int last = (L - 1) / kWRound;
+      const int n = min(L - last * kWRound, kWRound);
+      for (int u = 0; u * 4 * kWThreads < n; ++u)
+        sm100::mbar_wait(&s.vbar[u], static_cast<uint32_t>(last & 1), nullptr, kWaitTimeoutNs);
+    }
+  }
 
   if (!listed) {
     // More keys in the pivot bin than the list holds: the second digit over
@@ -759,7 +803,7 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   const bool small = n2 <= kSmall;
 
   // The pivot bin's entries: the list, or the row.
-  const int n3 = listed ? n1 : L;
+  const int n3 = listed ? min(s.cand_count, kWCap) : L;
   auto key_at = [&](int j) -> uint32_t {
     if (listed) return s.cand_key[j];
     const uint32_t key = ordered_key(row[j]);
@@ -905,15 +949,15 @@ __global__ void __launch_bounds__(kMThreads, 1)
     const bool gt = key != 0u && bb > bin1;
     const bool eq = use_cand && key != 0u && bb == bin1;
     const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-    if (gt) out[pos] = physical_id(bt_row, tokens[i]);
+    if (gt && pos < kTopK) out[pos] = physical_id(bt_row, tokens[i]);
     const int cpos = warp_alloc_n(&s.cand_count, eq ? 1 : 0);
-    if (eq) {
+    if (eq && cpos < kCandCap) {
       s.cand_key[cpos] = key;
       s.cand_idx[cpos] = i;
     }
   }
   __syncthreads();
-  const int m = use_cand ? s.cand_count : n;
+  const int m = use_cand ? min(s.cand_count, kCandCap) : n;
   auto bucket = [&](int j) -> uint32_t {  // key of the j-th pivot-bin entry, or 0
     if (j >= m) return 0u;
     if (use_cand) return s.cand_key[j];
@@ -955,9 +999,10 @@ __global__ void __launch_bounds__(kMThreads, 1)
     const bool gt = key != 0u && key > pivot;
     const bool eq = key != 0u && key == pivot;
     const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-    if (gt) out[pos] = physical_id(bt_row, tokens[index_of(j)]);
+    if (gt && pos < kTopK) out[pos] = physical_id(bt_row, tokens[index_of(j)]);
     const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
-    if (eq && ticket < k3) out[kTopK - k3 + ticket] = physical_id(bt_row, tokens[index_of(j)]);
+    const int slot = kTopK - k3 + ticket;
+    if (eq && ticket < k3 && slot >= 0 && slot < kTopK) out[slot] = physical_id(bt_row, tokens[index_of(j)]);
   }
 }
 

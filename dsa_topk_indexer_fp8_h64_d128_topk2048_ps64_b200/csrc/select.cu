@@ -620,15 +620,12 @@ template <bool kIds>
 __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectLaunch p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   WideSmem& s = *reinterpret_cast<WideSmem*>(smem_raw);
-  grid_dep_wait();
-  grid_dep_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31;
   const int b = blockIdx.x;
-  // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
-  // histogram (one coalesced 16-B load, issued before the row length is
-  // known), cleared for the next call once read.
-  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
-  const uint4 hx = g4[tid];
+  // Before the wait on the scoring kernel: what does not depend on it.  This
+  // kernel's predecessor in the stream is that scoring launch, which writes
+  // neither seq_lens nor the block table, and started its own work only after
+  // its predecessors had completed.
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
   const float* row = p.logits + static_cast<size_t>(b) * p.ld;
@@ -639,6 +636,7 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   out.offset = p.token_offset;
 
   if (L <= kTopK) {  // every token is selected
+    if constexpr (!kIds) grid_dep_wait();  // the pairs carry the scores
     for (int i = tid; i < kTopK; i += kWThreads) {
       if constexpr (kIds) {
         out.ids[i] = i < L ? physical_id(bt_row, i) : -1;
@@ -647,8 +645,34 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
         out.tokens[i] = i < L ? i + p.token_offset : -1;
       }
     }
+    // Every CTA waits before it ends, so that this grid completes only after
+    // the scoring grid (the next launch's wait relies on it).
+    if constexpr (kIds) grid_dep_wait();
+    grid_dep_launch_dependents();
     return;
   }
+  if (tid == 0) {
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) sm100::mbar_init(&s.vbar[u], 1);
+    sm100::fence_mbar_init();
+    s.out_count = 0;
+    s.cand_count = 0;
+    s.small_count = 0;
+    s.eq_count = 0;
+  }
+  const int npg = (L + kPage - 1) / kPage;
+  const bool bt_cached = kIds && npg <= kWBtCache;
+  if (bt_cached)
+    for (int i = tid; i < npg; i += kWThreads) s.bt[i] = bt_row[i];
+  s.hist[tid] = 0u;
+
+  // The scoring kernel's logits and histograms are complete past this wait.
+  grid_dep_wait();
+  grid_dep_launch_dependents();
+  // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
+  // histogram (one coalesced 16-B load), cleared for the next call once read.
+  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
+  const uint4 hx = g4[tid];
 
   // A round of logits into shared memory by thread 0: one bulk copy per
   // group of 4 * kWThreads entries, each on its own barrier, so that the
@@ -667,23 +691,7 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
       sm100::bulk_load(&s.vals[u][0], row + base + e0, bytes, &s.vbar[u], pol);
     }
   };
-  if (tid == 0) {
-#pragma unroll
-    for (int u = 0; u < kCPer / 4; ++u) sm100::mbar_init(&s.vbar[u], 1);
-    sm100::fence_mbar_init();
-    load_round(0);
-  }
-  const int npg = (L + kPage - 1) / kPage;
-  const bool bt_cached = kIds && npg <= kWBtCache;
-  if (bt_cached)
-    for (int i = tid; i < npg; i += kWThreads) s.bt[i] = bt_row[i];
-  s.hist[tid] = 0u;
-  if (tid == 0) {
-    s.out_count = 0;
-    s.cand_count = 0;
-    s.small_count = 0;
-    s.eq_count = 0;
-  }
+  if (tid == 0) load_round(0);
 
   uint32_t h1[4] = {hx.x, hx.y, hx.z, hx.w};
   if (tid == 0) s.extreme[0] = h1[0] != 0u;

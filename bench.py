@@ -47,6 +47,11 @@ from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import workloads as W  # n
 
 METRIC = "index-K HBM GB/s per indexer call (score + top-2048), B=64 decode"
 FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one score_kernel launch, from one ncu capture
+# of this bench's workload (dram__bytes_read.sum + dram__bytes_write.sum;
+# summary and command in profiles/score_kernel_config1.md).  Other configs
+# have no capture: their traffic is reported as null.
+SCORE_TRAFFIC_BYTES = {1: 156_324_096 + 4_711_168}
 N_SETS = 3
 
 
@@ -307,7 +312,11 @@ def bench_ours(args, world, rank, local):
                        "timing": f"CUDA events around each launch over {n_ev} further calls"},
         "roofline": {"kernel": "score_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                      "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "algorithmic_bytes_per_launch": sbytes, "traffic": None},
+                     "algorithmic_bytes_per_launch": sbytes,
+                     "traffic": SCORE_TRAFFIC_BYTES.get(args.config),
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                                        "(profiles/score_kernel_config1.md)" if args.config in SCORE_TRAFFIC_BYTES
+                                        else "no ncu capture for this config")},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": "kernel(...) drop-in, pinned host inputs"},

@@ -22,6 +22,8 @@ cpu_baseline: the CPU oracle (exact C restatement, all host threads) on a
            bounded sample of the same batch (rank 0, N = 1 only).
 --impl reference: the CPU implementation of the path (the oracle port) on
            the host cores, each step a bounded sample of the workload.
+--op write_k: the index-K cache writer (bf16 keys -> e4m3 pages) on
+           --tokens new tokens per call instead of the indexer.
 """
 from __future__ import annotations
 
@@ -451,6 +453,69 @@ def bench_reference(args, world, rank):
     }
 
 
+def bench_writer(args, world, rank, local):
+    """The index-K cache writer (dsai_write_k via write_index_k): n new bf16
+    keys quantised to e4m3 and scattered to shuffled physical slots of a pool
+    1.1x their size.  Algorithmic bytes per call: n x (256 B of bf16 keys +
+    4 B of slot id + 132 B of e4m3 row and scale).  Three rotating input
+    sets keep L2 from holding a previous call's data."""
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import write_index_k
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = args.tokens
+    pages = (n * 11 // 10 + 63) // 64
+    g = torch.Generator(device="cpu").manual_seed(7)
+    sets = []
+    for _ in range(N_SETS):
+        k = torch.randn((n, 128), generator=g).to(torch.bfloat16).to(dev)
+        ids = torch.randperm(pages * 64, generator=g)[:n].to(torch.int32).to(dev)
+        pool = torch.zeros((pages, 64, 1, 132), dtype=torch.uint8, device=dev)
+        sets.append((k, ids, pool))
+    alg = n * (256 + 4 + 132)
+    for i in range(args.warmup):
+        write_index_k(*sets[i % N_SETS])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        write_index_k(*sets[i % N_SETS])
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    gbs = alg / (ms / 1e3) / 1e9
+    peak, peak_src = measured_hbm_peak()
+    line = {
+        "metric": "index-K cache writer GB/s (bf16 keys -> e4m3 pages + fp32 scales)", "value": round(gbs, 1),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 5), "us_per_call": round(ms * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> e4m3 (fp32 scale)",
+        "data": "synthetic (seeded N(0,1) keys, shuffled slots)",
+        "config": {"workload": f"write_k: {n} new tokens into a {pages}-page pool",
+                   "l2": f"{N_SETS} rotating input sets of {(n * 392 + pages * 8448) / 1e6:.0f} MB"},
+        "roofline": {"kernel": "write_k_kernel", "bound": "hbm", "achieved": round(gbs, 1), "peak": peak,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "algorithmic_bytes_per_launch": alg, "traffic": None},
+        "gpu_launches": args.steps,
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        k, ids, pool = sets[0]
+        m = min(n, 16384)
+        kc = k[:m].float().cpu().numpy()
+        idc = ids[:m].cpu().numpy()
+        cache = np.zeros(pages * 8448, np.uint8)
+        t0 = time.perf_counter()
+        O.write_k(kc, idc, cache, pages)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(m * 392 / dt / 1e9, 4), "unit": "GB/s", "cores": 1,
+                                "kind": "port", "sample": f"first {m} of {n} tokens, C oracle writer, {dt:.3f} s"}
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -462,12 +527,17 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")
     ap.add_argument("--ref-step-budget", type=float, default=2.0, help="seconds per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k"],
+                    help="write_k: the index-K cache writer instead of the indexer")
+    ap.add_argument("--tokens", type=int, default=131072, help="new tokens per write_k call")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args)
     try:
-        if args.impl == "reference":
+        if args.op == "write_k":
+            line = bench_writer(args, world, rank, local) if rank == 0 else None
+        elif args.impl == "reference":
             line = bench_reference(args, world, rank)
         elif args.config == 3:
             line = bench_split(args, world, rank, local)

@@ -26,11 +26,13 @@ STATUS_SEQLEN_CLAMPED = 0x1
 STATUS_BAD_PAGE = 0x2
 STATUS_WAIT_TIMEOUT = 0x4
 FLAG_SCORE_ALL_ROWS = 0x1
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
 
 EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
     "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
-    "dsai_run_noalloc", "dsai_selftest_wait_timeout",
+    "dsai_run_noalloc", "dsai_selftest_wait_timeout", "dsai_write_k",
 )
 
 
@@ -83,6 +85,8 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.dsai_run_noalloc.restype = ctypes.c_int
         lib.dsai_selftest_wait_timeout.argtypes = [vp, ctypes.c_uint64, vp]
         lib.dsai_selftest_wait_timeout.restype = ctypes.c_int
+        lib.dsai_write_k.argtypes = [vp, i32, vp, i32, vp, i32, vp]
+        lib.dsai_write_k.restype = ctypes.c_int
         lib.dsai_read_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
         lib.dsai_read_status.restype = ctypes.c_int
         lib.dsai_last_error.argtypes = []

@@ -16,7 +16,7 @@ PKG_DIR = Path(__file__).resolve().parent
 REPO = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libdsai.so"
-SOURCES = ["score.cu", "select.cu", "api.cu", "noalloc.cu"]
+SOURCES = ["score.cu", "select.cu", "api.cu", "noalloc.cu", "writer.cu"]
 HEADERS = ["common.cuh", "sm100.cuh", "launch.h"]
 
 NVCC_FLAGS = [

@@ -65,6 +65,11 @@ cudaError_t launch_merge(const float* scores, const int32_t* tokens, int n_cand,
                          const int32_t* bt_row, int max_pages, const int32_t* seq_len,
                          int32_t* out, cudaStream_t stream);
 
+// Index-K cache writer (csrc/writer.cu): quantises n new keys (fp32, or bf16
+// when bf16) and stores them at their physical slot ids.
+cudaError_t launch_write_k(const void* k_new, bool bf16, const int32_t* slot_ids, int n, uint8_t* k_cache,
+                           int num_pages, cudaStream_t stream);
+
 // Records `msg` as the calling thread's dsai_last_error() and returns code.
 int set_last_error(int code, const char* msg);
 

@@ -19,7 +19,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status"]
+__all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status", "write_index_k"]
 
 _FP8 = getattr(torch, "float8_e4m3fn", None)
 
@@ -156,6 +156,34 @@ def merge_pairs(scores: torch.Tensor, tokens: torch.Tensor, block_table_row: tor
         _lib.check(lib.dsai_merge_pairs(scores.data_ptr(), tokens.data_ptr(), int(scores.numel()),
                                         block_table_row.data_ptr(), int(block_table_row.numel()),
                                         seq_len.data_ptr(), out.data_ptr(), stream))
+
+
+def write_index_k(k_new: torch.Tensor, slot_ids: torch.Tensor, k_index_cache_fp8: torch.Tensor) -> None:
+    """Index-K cache writer (the step before the indexer in a decode step):
+    quantises the new keys ``k_new`` ([n, 128] float32 or bfloat16) to e4m3
+    with one fp32 scale per token (max |k| / 448) and stores token i at
+    physical slot id ``slot_ids[i]`` (int32 page*64 + slot, -1 = skip) of
+    ``k_index_cache_fp8`` ([num_pages, 64, 1, 132] uint8), in the page layout
+    ``kernel`` reads.  Runs on the current stream; no host synchronisation."""
+    _req(k_new.is_cuda and k_new.is_contiguous() and k_new.dtype in (torch.float32, torch.bfloat16),
+         "k_new must be float32 or bfloat16 contiguous CUDA")
+    _req(k_new.dim() == 2 and k_new.size(1) == _lib.HEAD_DIM, "k_new shape must be [n, 128]")
+    _check_int32(slot_ids, "slot_ids")
+    _req(slot_ids.numel() == k_new.size(0), "slot_ids must hold one id per new token")
+    _req(k_index_cache_fp8.is_cuda and k_index_cache_fp8.is_contiguous()
+         and k_index_cache_fp8.element_size() == 1 and k_index_cache_fp8.numel() % _lib.PAGE_BYTES == 0,
+         "k_index_cache_fp8 must be uint8 contiguous CUDA [num_pages, 64, 1, 132]")
+    n = int(k_new.size(0))
+    if n == 0:
+        return
+    lib = _lib.load_library()
+    dev = k_new.device
+    dtype = _lib.DTYPE_BF16 if k_new.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    with torch.cuda.device(dev):
+        _lib.check(lib.dsai_write_k(k_new.data_ptr(), dtype, slot_ids.data_ptr(), n,
+                                    k_index_cache_fp8.data_ptr(),
+                                    int(k_index_cache_fp8.numel() // _lib.PAGE_BYTES),
+                                    torch.cuda.current_stream(dev).cuda_stream))
 
 
 def read_status(device=None) -> int:

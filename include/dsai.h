@@ -52,6 +52,10 @@ extern "C" {
 #define DSAI_E_CUDA (-3)      /* a CUDA runtime / driver call failed */
 #define DSAI_E_UNSUPPORTED (-4) /* device is not sm_100 or the library was built without it */
 
+/* Element types of dsai_write_k's new keys. */
+#define DSAI_DTYPE_F32 0
+#define DSAI_DTYPE_BF16 1
+
 /* Device status bits, accumulated in the workspace header by the kernels and
  * read with dsai_read_status().  They never stop a call: the kernels clamp
  * or zero-fill and carry on, so the output stays well defined. */
@@ -126,6 +130,19 @@ DSAI_API int dsai_merge_pairs(const float* scores, const int32_t* tokens, int32_
  * work can overlap on the GPU race and must be serialised.  No counterpart
  * in the reference. */
 DSAI_API int dsai_run_noalloc(const dsai_args* args, void* stream);
+
+/* Index-K cache writer: quantises n_tokens new keys k_new [n_tokens, 128]
+ * (fp32 or bf16, row-major) to e4m3 with one fp32 scale per token
+ * (scale = max(max_d |k|, 1e-12) / 448, values clamp(k / scale, +-448),
+ * round to nearest even) and stores token i at physical slot id
+ * slot_ids[i] = page*64 + slot of k_cache (the page layout above): 128 bytes
+ * at page*8448 + slot*128 and the scale at page*8448 + 8192 + slot*4.  Ids of
+ * -1 and ids outside [0, num_pages*64) are skipped.  k_new 16-B (fp32) or
+ * 8-B (bf16) aligned, k_cache 16-B aligned.  Two tokens with the same id race.
+ * No counterpart in the reference, which reads this cache but does not
+ * write it; the format is the one it reads (solution/python/kernel.cu:29-40). */
+DSAI_API int dsai_write_k(const void* k_new, int32_t dtype, const int32_t* slot_ids, int32_t n_tokens,
+                          void* k_cache, int32_t num_pages, void* stream);
 
 /* Copy the workspace status word to *status_out (host), then clear it.
  * Synchronises `stream`. */

@@ -277,3 +277,58 @@ int dsai_oracle_merge(const float* scores, const int32_t* tokens, int n_cand,
   free(e);
   return 0;
 }
+
+/* ---------------------------------------------------------------- writer
+ * CPU restatement of the index-K cache writer (the step that produces the
+ * page layout above; the reference reads this format, solution/python/
+ * kernel.cu:29-40, but has no writer).  Per token: amax = max |k| (at least
+ * 1e-12), scale = amax / 448 in fp32, values clamp(k / scale, -448, 448)
+ * rounded to e4m3 (round to nearest, ties to even).  The encoder follows the
+ * e4m3 format definition: 1 sign bit, 4 exponent bits (bias 7), 3 mantissa
+ * bits; exponent field 0 holds subnormals m * 2^-9; the largest finite value
+ * is 448 (exponent 15, mantissa 6); exponent 15 with mantissa 7 is NaN. */
+uint8_t dsai_oracle_e4m3_encode(float x) {
+  const uint8_t sign = signbit(x) ? 0x80 : 0x00;
+  double a = fabs((double)x);
+  if (a > 448.0) a = 448.0;
+  if (a == 0.0) return sign;
+  unsigned code;
+  if (a < ldexp(1.0, -6)) {          /* subnormal range: quantum 2^-9 */
+    code = (unsigned)nearbyint(a * 512.0);  /* 8 carries into the smallest normal */
+  } else {
+    int e;
+    (void)frexp(a, &e);              /* a in [2^(e-1), 2^e) */
+    e -= 1;                          /* a in [2^e, 2^(e+1)) */
+    unsigned q = (unsigned)nearbyint(ldexp(a, 3 - e));  /* in [8, 16] */
+    if (q == 16) { q = 8; e += 1; }
+    code = ((unsigned)(e + 7) << 3) | (q - 8);
+  }
+  if (code > 0x7E) code = 0x7E;      /* saturate at 448 */
+  return (uint8_t)(sign | code);
+}
+
+int dsai_oracle_write_k(const float* k, int n, const int32_t* slot_ids, uint8_t* k_cache, int num_pages) {
+  const long long num_slots = (long long)num_pages * PS;
+  for (int i = 0; i < n; ++i) {
+    const int32_t sid = slot_ids[i];
+    if (sid < 0 || (long long)sid >= num_slots) continue;
+    const float* v = k + (size_t)i * HD;
+    float amax = 0.0f;
+    for (int d = 0; d < HD; ++d) {
+      const float m = fabsf(v[d]);
+      if (m > amax) amax = m;
+    }
+    if (amax < 1e-12f) amax = 1e-12f;
+    const float scale = amax / 448.0f;
+    uint8_t* pg = k_cache + (size_t)(sid / PS) * PAGE_BYTES;
+    const int slot = sid % PS;
+    for (int d = 0; d < HD; ++d) {
+      float x = v[d] / scale;
+      if (x > 448.0f) x = 448.0f;
+      if (x < -448.0f) x = -448.0f;
+      pg[slot * HD + d] = dsai_oracle_e4m3_encode(x);
+    }
+    memcpy(pg + 8192 + 4 * slot, &scale, 4);
+  }
+  return 0;
+}

@@ -62,6 +62,10 @@ def lib() -> ctypes.CDLL:
         L.dsai_oracle_pairs.argtypes = [vp, vp, i32, i32, ctypes.c_int32, vp, vp]
         L.dsai_oracle_pairs.restype = i32
         L.dsai_oracle_merge.argtypes = [vp, vp, i32, vp, i32, ctypes.c_int32, vp]
+        L.dsai_oracle_e4m3_encode.argtypes = [ctypes.c_float]
+        L.dsai_oracle_e4m3_encode.restype = ctypes.c_uint8
+        L.dsai_oracle_write_k.argtypes = [vp, i32, vp, vp, i32]
+        L.dsai_oracle_write_k.restype = ctypes.c_int
         L.dsai_oracle_merge.restype = i32
         _lib = L
     return _lib
@@ -135,6 +139,21 @@ def merge(scores, tokens, block_table_row, seq_len):
 
 
 # ----------------------------------------------------------------- numpy form
+def e4m3_encode(x: float) -> int:
+    """e4m3 byte of one fp32 value (round to nearest even, saturating at 448)."""
+    return int(lib().dsai_oracle_e4m3_encode(float(x)))
+
+
+def write_k(k: np.ndarray, slot_ids: np.ndarray, k_cache: np.ndarray, num_pages: int) -> None:
+    """Index-K cache writer, in place on k_cache (uint8, num_pages*8448 bytes):
+    k [n, 128] fp32 new keys, slot_ids [n] int32 physical ids."""
+    k = _c(k, np.float32)
+    ids = _c(slot_ids, np.int32)
+    assert k_cache.dtype == np.uint8 and k_cache.flags["C_CONTIGUOUS"]
+    assert k.ndim == 2 and k.shape[1] == 128 and ids.shape[0] == k.shape[0]
+    lib().dsai_oracle_write_k(_p(k), k.shape[0], _p(ids), _p(k_cache), int(num_pages))
+
+
 def _e4m3_numpy() -> np.ndarray:
     """e4m3 decode written independently of the C code (sign, 4-bit
     exponent with bias 7, 3-bit mantissa, subnormals, NaN at 0x7F/0xFF)."""

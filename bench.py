@@ -24,6 +24,8 @@ cpu_baseline: the CPU oracle (exact C restatement, all host threads) on a
            the host cores, each step a bounded sample of the workload.
 --op write_k: the index-K cache writer (bf16 keys -> e4m3 pages) on
            --tokens new tokens per call instead of the indexer.
+--op graph: small-batch latency (config 0), kernel(...) called eagerly
+           against the same call replayed from a CUDA graph (IndexerGraph).
 """
 from __future__ import annotations
 
@@ -516,6 +518,49 @@ def bench_writer(args, world, rank, local):
     return line
 
 
+def bench_graph(args, world, rank, local):
+    """Small-batch latency: the drop-in kernel(...) called eagerly against
+    the same call captured once (IndexerGraph) and replayed, both timed over
+    K back-to-back calls with CUDA events.  Workload: benchmark config 0
+    (B=2, seq_lens {1500, 4096}, 64 pages per row), where per-call host work
+    dominates."""
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import IndexerGraph
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = W.config_inputs(0, device=dev)
+    out = g.out()
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps * 1e3
+
+    eager_us = timed(lambda: kernel(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out))
+    graph = IndexerGraph(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out)
+    clocks = ClockSampler(dev)
+    clocks.start()
+    graph_us = timed(graph.replay)
+    clk = clocks.stop()
+    return {
+        "metric": "us per indexer call, config 0 (B=2), CUDA-graph replay", "value": round(graph_us, 2),
+        "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(graph_us / 1e3, 5), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "e4m3 x e4m3 -> f32 (scores), u32 keys (select)",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": f"config0: {W.CONFIGS[0]}", "rows": g.rows, "max_pages": g.max_pages},
+        "eager_us_per_call": round(eager_us, 2),
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -527,8 +572,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")
     ap.add_argument("--ref-step-budget", type=float, default=2.0, help="seconds per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k"],
-                    help="write_k: the index-K cache writer instead of the indexer")
+    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k", "graph"],
+                    help="write_k: the index-K cache writer; graph: small-batch latency, eager vs CUDA graph")
     ap.add_argument("--tokens", type=int, default=131072, help="new tokens per write_k call")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -537,6 +582,8 @@ def main():
     try:
         if args.op == "write_k":
             line = bench_writer(args, world, rank, local) if rank == 0 else None
+        elif args.op == "graph":
+            line = bench_graph(args, world, rank, local) if rank == 0 else None
         elif args.impl == "reference":
             line = bench_reference(args, world, rank)
         elif args.config == 3:

@@ -56,6 +56,7 @@ FALLBACK_HBM_GBS = 6650.0
 # summary and command in profiles/score_kernel_config1.md).  Other configs
 # have no capture: their traffic is reported as null.
 SCORE_TRAFFIC_BYTES = {1: 156_324_096 + 4_711_168}
+SCORE_PROFILE = {1: "score_kernel_config1.md"}
 N_SETS = 3
 
 
@@ -70,10 +71,38 @@ def measured_hbm_peak():
 
 def score_bytes(inp) -> int:
     """Algorithmic bytes of the scoring kernel: per scored row 132*L (K +
-    scale) + 4*ceil(L/64) (block table) + 8192 (q) + 256 (weights) + 4."""
+    scale) + 4*ceil(L/64) (block table) + 8192 (q) + 256 (weights) + 4.
+    With rows_per_seq = R > 1 the K + scale and block-table bytes count once
+    per group of R rows, for its longest row."""
     sl = np.clip(inp.seq_lens.cpu().numpy().astype(np.int64), 0, inp.max_pages * 64)
-    sl = sl[sl > 2048]
-    return int((132 * sl + 4 * ((sl + 63) // 64) + 8192 + 256 + 4).sum())
+    R = max(1, inp.rows_per_seq)
+    if R == 1:
+        sl = sl[sl > 2048]
+        return int((132 * sl + 4 * ((sl + 63) // 64) + 8192 + 256 + 4).sum())
+    lmax = sl.reshape(-1, R).max(axis=1)
+    lmax = lmax[lmax > 2048]
+    return int((132 * lmax + 4 * ((lmax + 63) // 64) + R * (8192 + 256 + 4)).sum())
+
+
+def score_flops(inp) -> int:
+    """Algorithmic tensor flops of the scoring kernel: 2 * 64 heads * 128
+    dims per scored (row, token) pair, each row over its own length."""
+    sl = np.clip(inp.seq_lens.cpu().numpy().astype(np.int64), 0, inp.max_pages * 64)
+    R = max(1, inp.rows_per_seq)
+    scored = np.repeat(sl.reshape(-1, R).max(axis=1) > 2048, R)
+    return int(2 * 64 * 128 * sl[scored].sum())
+
+
+def measured_fp8_peak():
+    """Dense fp8 tensor peak: twice the measured cuBLAS bf16 burst rate (the
+    fp8 rate of B200's tensor cores is twice its bf16 rate; no fp8 GEMM is
+    measured on this pool)."""
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return 2.0 * float(d["bf16_tflops"]), "2 x measured bf16 burst (MEASURED_PEAKS.json bf16_tflops)"
+    except Exception:
+        return 2.0 * 1590.0, "2 x fallback bf16 1.59 PFLOP/s"
 
 
 class ClockSampler:
@@ -142,7 +171,8 @@ def parity_guard(inp) -> None:
     kernel's own logits.  Runs once, outside the timed region, on torch."""
     out = inp.out()
     lg = torch.full((inp.rows, inp.max_pages * 64), float("nan"), device=inp.q.device)
-    run(inp.q, inp.k_cache, inp.weights, inp.seq_lens, inp.block_table, out, logits_out=lg)
+    run(inp.q, inp.k_cache, inp.weights, inp.seq_lens, inp.block_table, out, logits_out=lg,
+        rows_per_seq=inp.rows_per_seq)
     torch.cuda.synchronize()
     st = read_status(inp.q.device)
     if st != 0:
@@ -184,10 +214,12 @@ def cpu_oracle_sample(inp_cpu: W.Inputs, budget_s: float):
         return time.perf_counter() - t0
 
     t1 = run_rows(1)
+    R = max(1, inp_cpu.rows_per_seq)
     n = int(max(1, min(inp_cpu.rows, budget_s / max(t1, 1e-3))))
+    n = max(R, n - n % R)  # whole groups, so the sample's bytes count K once per group too
     dt = run_rows(n) if n > 1 else t1
     sub = W.Inputs(inp_cpu.q[:n], inp_cpu.k_cache, inp_cpu.weights[:n], inp_cpu.seq_lens[:n],
-                   inp_cpu.block_table[:n])
+                   inp_cpu.block_table[:n], rows_per_seq=R)
     return sub.algorithmic_bytes() / dt / 1e9, n, dt, threads
 
 
@@ -207,8 +239,12 @@ def bench_ours(args, world, rank, local):
     torch.cuda.set_device(dev)
     seed = 100 * args.config + rank
     base = W.config_inputs(args.config, seed=seed, device=dev)
+    if args.rows_per_seq:
+        base.rows_per_seq = args.rows_per_seq
     sets = [base] + [W.Inputs(base.q.clone(), base.k_cache.clone(), base.weights.clone(), base.seq_lens.clone(),
-                              base.block_table.clone(), base.name, base.seed) for _ in range(N_SETS - 1)]
+                              base.block_table.clone(), base.name, base.seed, rows_per_seq=base.rows_per_seq)
+                     for _ in range(N_SETS - 1)]
+    R = base.rows_per_seq
     outs = [s.out() for s in sets]
     parity_guard(base)
     alg = base.algorithmic_bytes()
@@ -217,7 +253,8 @@ def bench_ours(args, world, rank, local):
 
     def step(i, ev=None):
         s = sets[i % N_SETS]
-        run(s.q, s.k_cache, s.weights, s.seq_lens, s.block_table, outs[i % N_SETS], event_after_score=ev)
+        run(s.q, s.k_cache, s.weights, s.seq_lens, s.block_table, outs[i % N_SETS], event_after_score=ev,
+            rows_per_seq=R)
 
     for i in range(args.warmup):
         step(i)
@@ -276,7 +313,11 @@ def bench_ours(args, world, rank, local):
     def e2e_step():
         for k, v in host.items():
             devb[k].copy_(v, non_blocking=True)
-        kernel(devb["q"], devb["k_cache"], devb["weights"], devb["seq_lens"], devb["block_table"], out_d)
+        if R == 1:
+            kernel(devb["q"], devb["k_cache"], devb["weights"], devb["seq_lens"], devb["block_table"], out_d)
+        else:
+            run(devb["q"], devb["k_cache"], devb["weights"], devb["seq_lens"], devb["block_table"], out_d,
+                rows_per_seq=R)
         out_h.copy_(out_d, non_blocking=True)
 
     for _ in range(min(3, args.warmup)):
@@ -300,12 +341,34 @@ def bench_ours(args, world, rank, local):
         return None
     peak, peak_src = measured_hbm_peak()
     achieved = sbytes / (score_ms / 1e3) / 1e9
+    kname = "score_kernel" if R == 1 else f"score_mq_kernel<{R}>"
+    roof = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+            "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "algorithmic_bytes_per_launch": sbytes,
+            "traffic": SCORE_TRAFFIC_BYTES.get(args.config) if R == base.rows_per_seq else None,
+            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
+                               f"(profiles/{SCORE_PROFILE.get(args.config, '')})" if args.config in SCORE_TRAFFIC_BYTES
+                               else "no ncu capture for this config")}
+    flops = score_flops(base)
+    tpeak, tpeak_src = measured_fp8_peak()
+    tensor = {"achieved": round(flops / (score_ms / 1e3) / 1e12, 1), "peak": round(tpeak, 1),
+              "peak_source": tpeak_src, "unit": "TFLOP/s", "algorithmic_flops_per_launch": flops}
+    tensor["frac"] = round(tensor["achieved"] / tpeak, 4)
+    if flops / (tpeak * 1e12) > sbytes / (peak * 1e9):
+        # the tensor pipe bounds this workload: report it as the roofline
+        other = {k: roof[k] for k in ("achieved", "peak", "peak_source", "unit", "frac")}
+        roof.update(bound="tensor", **{k: tensor[k] for k in ("achieved", "peak", "peak_source", "unit", "frac")})
+        roof["algorithmic_flops_per_launch"] = flops
+        roof["hbm"] = other
+    else:
+        roof["tensor"] = tensor
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> f32 (scores), u32 keys (select)", "data": "synthetic (seeded, generated on device)",
         "config": {"workload": f"config{args.config}: {W.CONFIGS[args.config]}", "rows_per_gpu": base.rows,
+                   "rows_per_seq": R,
                    "scored_tokens_per_gpu": tokens, "pool_pages": base.num_pages, "max_pages": base.max_pages,
                    "seed": seed, "l2": f"{N_SETS} rotating input copies of {base.k_cache.numel() / 1e6:.0f} MB K pool (> 126 MB L2)",
                    "parallelism": f"rows sharded, dp{world}" if world > 1 else "single GPU"},
@@ -314,16 +377,10 @@ def bench_ours(args, world, rank, local):
         "frac_of_8tbs": round(value / world / 8000.0, 4),
         "kernels_ms": {"score": round(score_ms, 5), "select": round(select_ms, 5),
                        "timing": f"CUDA events around each launch over {n_ev} further calls"},
-        "roofline": {"kernel": "score_kernel", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                     "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "algorithmic_bytes_per_launch": sbytes,
-                     "traffic": SCORE_TRAFFIC_BYTES.get(args.config),
-                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                                        "(profiles/score_kernel_config1.md)" if args.config in SCORE_TRAFFIC_BYTES
-                                        else "no ncu capture for this config")},
+        "roofline": roof,
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "path": "kernel(...) drop-in, pinned host inputs"},
+                "path": ("kernel(...) drop-in" if R == 1 else f"run(..., rows_per_seq={R})") + ", pinned host inputs"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk,
     }
@@ -434,8 +491,11 @@ def bench_reference(args, world, rank):
 
     budget = args.ref_step_budget
     t1 = one(1)
+    R = max(1, inp.rows_per_seq)
     n = int(max(1, min(inp.rows, budget / max(t1, 1e-3))))
-    sub = W.Inputs(inp.q[:n], inp.k_cache, inp.weights[:n], inp.seq_lens[:n], inp.block_table[:n])
+    n = max(R, n - n % R)  # whole groups of rows that share a sequence
+    sub = W.Inputs(inp.q[:n], inp.k_cache, inp.weights[:n], inp.seq_lens[:n], inp.block_table[:n],
+                   rows_per_seq=R)
     alg = sub.algorithmic_bytes()
     for _ in range(args.warmup):
         one(n)
@@ -567,6 +627,8 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--rows-per-seq", type=int, default=0,
+                    help="override the config's rows per sequence (1 scores config 4 row by row)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")

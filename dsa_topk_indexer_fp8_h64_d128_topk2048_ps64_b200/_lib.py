@@ -28,6 +28,10 @@ STATUS_WAIT_TIMEOUT = 0x4
 FLAG_SCORE_ALL_ROWS = 0x1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+E_INVALID = -1      # DSAI_E_* return codes
+E_WORKSPACE = -2
+E_CUDA = -3
+E_UNSUPPORTED = -4
 
 EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
@@ -51,6 +55,7 @@ class DsaiArgs(ctypes.Structure):
         ("num_pages", ctypes.c_int32),
         ("flags", ctypes.c_int32),
         ("ev_after_score", ctypes.c_void_p),
+        ("rows_per_seq", ctypes.c_int32),
     ]
 
 

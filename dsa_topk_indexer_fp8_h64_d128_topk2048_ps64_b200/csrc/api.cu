@@ -198,6 +198,10 @@ int check_args(const dsai_args* a, void* ws, size_t ws_bytes, bool need_ids) {
   if (a->rows < 0 || a->max_pages < 0 || a->num_pages < 0)
     return fail(DSAI_E_INVALID, "negative size (rows=%d max_pages=%d num_pages=%d)", a->rows,
                 a->max_pages, a->num_pages);
+  if (a->rows_per_seq < 0 || a->rows_per_seq > 4)
+    return fail(DSAI_E_INVALID, "rows_per_seq must be 0 to 4 (got %d)", a->rows_per_seq);
+  if (a->rows_per_seq > 1 && a->rows % a->rows_per_seq != 0)
+    return fail(DSAI_E_INVALID, "rows (%d) must be a multiple of rows_per_seq (%d)", a->rows, a->rows_per_seq);
   if (a->rows == 0) return DSAI_OK;
   if (!a->seq_lens || !a->block_table) return fail(DSAI_E_INVALID, "seq_lens / block_table is NULL");
   if (need_ids && !a->topk_indices) return fail(DSAI_E_INVALID, "topk_indices is NULL");
@@ -232,8 +236,10 @@ int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, 
   rc = get_map(kMapS, a->k_cache, static_cast<uint64_t>(a->num_pages), &ts);
   if (rc) return rc;
   const int ld = a->max_pages * dsai::kPage;
-  for (int r0 = 0; r0 < a->rows; r0 += dsai::kMaxRowsPerLaunch) {
-    const int n = a->rows - r0 < dsai::kMaxRowsPerLaunch ? a->rows - r0 : dsai::kMaxRowsPerLaunch;
+  const int group = a->rows_per_seq > 1 ? a->rows_per_seq : 1;
+  const int chunk = (dsai::kMaxRowsPerLaunch / group) * group;  // launches never split a group
+  for (int r0 = 0; r0 < a->rows; r0 += chunk) {
+    const int n = a->rows - r0 < chunk ? a->rows - r0 : chunk;
     dsai::ScoreLaunch p;
     p.weights = a->weights + static_cast<size_t>(r0) * dsai::kHeads;
     p.seq_lens = a->seq_lens + r0;
@@ -248,7 +254,8 @@ int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, 
     p.row_base = r0;
     p.score_all = score_all ? 1 : 0;
     p.grid = sms;
-    cudaError_t e = dsai::launch_score(p, tq, tk, ts, stream);
+    cudaError_t e = group > 1 ? dsai::launch_score_groups(p, group, tq, tk, ts, stream)
+                              : dsai::launch_score(p, tq, tk, ts, stream);
     if (e != cudaSuccess) return cuda_fail(e, "score kernel launch");
   }
   return DSAI_OK;

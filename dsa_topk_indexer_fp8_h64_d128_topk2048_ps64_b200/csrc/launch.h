@@ -29,6 +29,13 @@ struct ScoreLaunch {
 cudaError_t launch_score(const ScoreLaunch& p, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
                          const CUtensorMap& tmap_s, cudaStream_t stream);
 
+// The same scoring for groups of `rows_per_group` (2-4) consecutive rows that
+// read one block-table row (the group's longest row's): each K tile is staged
+// once and multiplied against the whole group.  `p.rows` is a multiple of
+// rows_per_group; `p.grid` is the number of CTAs (one per SM).
+cudaError_t launch_score_groups(const ScoreLaunch& p, int rows_per_group, const CUtensorMap& tmap_q,
+                                const CUtensorMap& tmap_k, const CUtensorMap& tmap_s, cudaStream_t stream);
+
 struct SelectLaunch {
   const float* logits;  // [rows, ld]
   int ld;

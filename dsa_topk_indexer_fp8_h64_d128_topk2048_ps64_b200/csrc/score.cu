@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "sm100.cuh"
+#include "tiles.cuh"
 
 namespace dsai {
 namespace {
@@ -86,38 +87,6 @@ struct ScoreSmem {
 
 constexpr int kSmemBytes = static_cast<int>(sizeof(ScoreSmem)) + 1024;
 static_assert(kCtasPerSm * (kSmemBytes + 1024) <= 233472, "two CTAs per SM must fit");
-
-// Last row r with row_start[r] <= t (t < row_start[rows]); that row is the
-// non-empty row holding tile t.
-__device__ __forceinline__ int find_row(const int* rs, int rows, int t) {
-  int lo = 0, hi = rows - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (rs[mid] <= t) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-// Walks the tiles of a CTA's slice in order, tracking the row.
-struct Cursor {
-  int t, row, j, row_end;
-  __device__ void init(const int* rs, int rows, int t0) {
-    t = t0;
-    row = find_row(rs, rows, t0);
-    j = t0 - rs[row];
-    row_end = rs[row + 1];
-  }
-  __device__ void next(const int* rs, int t1) {
-    ++t;
-    ++j;
-    if (t < t1 && t == row_end) {
-      ++row;
-      while (rs[row + 1] <= t) ++row;
-      j = 0;
-      row_end = rs[row + 1];
-    }
-  }
-};
 
 __device__ __forceinline__ void fail(ScoreSmem& s, int* status) {
   report(status, DSAI_STATUS_WAIT_TIMEOUT);
@@ -389,22 +358,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const float sc = s.scale[sslot][tok];
         __syncwarp();
         if (lane == 0) mbar_arrive(&s.sempty[sslot]);
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        // Eight running sums: a_c over heads 4i + c, b_c over 32 + 4i + c,
+        // then ((a0+b0)+(a1+b1)) + ((a2+b2)+(a3+b3)) (the group scorer's order).
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
 #pragma unroll
         for (int h = 0; h < 32; h += 4) {
           a0 = fmaf(fmaxf(__uint_as_float(r0[h + 0]), 0.f), w[h + 0], a0);
           a1 = fmaf(fmaxf(__uint_as_float(r0[h + 1]), 0.f), w[h + 1], a1);
           a2 = fmaf(fmaxf(__uint_as_float(r0[h + 2]), 0.f), w[h + 2], a2);
           a3 = fmaf(fmaxf(__uint_as_float(r0[h + 3]), 0.f), w[h + 3], a3);
+          b0 = fmaf(fmaxf(__uint_as_float(r1[h + 0]), 0.f), w[32 + h + 0], b0);
+          b1 = fmaf(fmaxf(__uint_as_float(r1[h + 1]), 0.f), w[32 + h + 1], b1);
+          b2 = fmaf(fmaxf(__uint_as_float(r1[h + 2]), 0.f), w[32 + h + 2], b2);
+          b3 = fmaf(fmaxf(__uint_as_float(r1[h + 3]), 0.f), w[32 + h + 3], b3);
         }
-#pragma unroll
-        for (int h = 0; h < 32; h += 4) {
-          a0 = fmaf(fmaxf(__uint_as_float(r1[h + 0]), 0.f), w[32 + h + 0], a0);
-          a1 = fmaf(fmaxf(__uint_as_float(r1[h + 1]), 0.f), w[32 + h + 1], a1);
-          a2 = fmaf(fmaxf(__uint_as_float(r1[h + 2]), 0.f), w[32 + h + 2], a2);
-          a3 = fmaf(fmaxf(__uint_as_float(r1[h + 3]), 0.f), w[32 + h + 3], a3);
-        }
-        const float logit = ((a0 + a1) + (a2 + a3)) * sc;
+        const float logit = (((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3))) * sc;
         const int t_abs = c.j * kTileTok + tok;
         const bool live = t_abs < L;
         if (live) out_row[t_abs] = logit;

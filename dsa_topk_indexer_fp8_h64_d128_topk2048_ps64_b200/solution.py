@@ -46,7 +46,7 @@ def _check_scoring_inputs(q, k, w, rows: int) -> None:
     _req(w.numel() == rows * _lib.NUM_HEADS, "weights shape must be [B, 64]")
 
 
-def _args(q, k, w, seq_lens, block_table, out, logits_out, flags: int) -> _lib.DsaiArgs:
+def _args(q, k, w, seq_lens, block_table, out, logits_out, flags: int, rows_per_seq: int = 1) -> _lib.DsaiArgs:
     rows, max_pages = int(block_table.size(0)), int(block_table.size(1))
     a = _lib.DsaiArgs()
     a.q = q.data_ptr() if q is not None else None
@@ -61,17 +61,24 @@ def _args(q, k, w, seq_lens, block_table, out, logits_out, flags: int) -> _lib.D
     a.num_pages = (k.numel() // _lib.PAGE_BYTES) if k is not None else 0
     a.flags = flags
     a.ev_after_score = None
+    a.rows_per_seq = rows_per_seq
     return a
 
 
 def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices,
         logits_out: torch.Tensor | None = None, score_all_rows: bool = False,
-        event_after_score: torch.cuda.Event | None = None, workspace: "_lib.Workspace | None" = None):
+        event_after_score: torch.cuda.Event | None = None, workspace: "_lib.Workspace | None" = None,
+        rows_per_seq: int = 1):
     """The indexer with optional extras: ``logits_out`` ([B, max_pages*64]
     fp32) receives the scored logits (entries at t >= seq_len are left
     untouched; rows with seq_len <= 2048 are scored only with
     ``score_all_rows``), ``event_after_score`` is recorded between the
-    scoring and the selection launches."""
+    scoring and the selection launches.  ``rows_per_seq`` = 2..4 declares
+    consecutive groups of that many rows to be query tokens of one sequence
+    (multi-query decode, next-n / MTP, causal prefill rows) that agree on
+    ``block_table`` over every page each of them reaches: each group's K
+    pages are then read once, through the block-table row of its longest
+    row.  The results are those of independent rows."""
     _check_int32(block_table, "block_table")
     _check_int32(seq_lens, "seq_lens")
     _check_int32(topk_indices, "topk_indices")
@@ -79,6 +86,8 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
     _req(topk_indices.dim() == 2 and topk_indices.size(0) == rows and topk_indices.size(1) == _lib.TOPK,
          "topk_indices shape must be [B, 2048]")
     _req(seq_lens.numel() == rows, "seq_lens shape must be [B]")
+    _req(isinstance(rows_per_seq, int) and 1 <= rows_per_seq <= 4, "rows_per_seq must be 1 to 4")
+    _req(rows % rows_per_seq == 0, "rows must be a multiple of rows_per_seq")
     if rows == 0:
         return
     lib = _lib.load_library()
@@ -95,7 +104,7 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
     ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
     a = _args(q_index_fp8 if needs_scoring else None, k_index_cache_fp8 if needs_scoring else None,
               weights if needs_scoring else None, seq_lens, block_table, topk_indices, logits_out,
-              _lib.FLAG_SCORE_ALL_ROWS if score_all_rows else 0)
+              _lib.FLAG_SCORE_ALL_ROWS if score_all_rows else 0, rows_per_seq)
     if needs_scoring:
         a.num_pages = k_index_cache_fp8.numel() // _lib.PAGE_BYTES
     if event_after_score is not None:
@@ -204,22 +213,25 @@ class IndexerGraph:
     replays; shapes and addresses are fixed.  ``replay()`` launches the two
     kernels on the current stream with one graph launch, which removes the
     per-call host work of ``kernel()`` (argument checks, ctypes call, two
-    launches) that dominates on small batches."""
+    launches) that dominates on small batches.  ``rows_per_seq`` is that of
+    ``run``."""
 
-    def __init__(self, q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):
+    def __init__(self, q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices,
+                 rows_per_seq: int = 1):
         self.tensors = (q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)
+        self.rows_per_seq = rows_per_seq
         dev = block_table.device
         self.workspace = _lib.Workspace(dev)
         side = torch.cuda.Stream(dev)
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
             # sizes the workspace, encodes the tensor maps, sets kernel attributes
-            run(*self.tensors, workspace=self.workspace)
+            run(*self.tensors, workspace=self.workspace, rows_per_seq=rows_per_seq)
         torch.cuda.current_stream(dev).wait_stream(side)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
-            run(*self.tensors, workspace=self.workspace)
+            run(*self.tensors, workspace=self.workspace, rows_per_seq=rows_per_seq)
 
     def replay(self) -> None:
         """Runs the captured call on the current stream."""

@@ -31,6 +31,7 @@ class Inputs:
     name: str = ""
     seed: int = 0
     planted: dict = field(default_factory=dict)  # row -> list of planted token indices
+    rows_per_seq: int = 1      # consecutive rows sharing one sequence's block-table row
 
     @property
     def rows(self) -> int:
@@ -50,7 +51,7 @@ class Inputs:
     def to(self, device) -> "Inputs":
         return Inputs(self.q.to(device), self.k_cache.to(device), self.weights.to(device),
                       self.seq_lens.to(device), self.block_table.to(device), self.name, self.seed,
-                      dict(self.planted))
+                      dict(self.planted), self.rows_per_seq)
 
     def numpy(self) -> dict:
         """Host copies for the CPU oracle (q and k as raw bytes)."""
@@ -65,13 +66,24 @@ class Inputs:
         """Bytes the operator must move per call: per scored row 132*L of
         index-K + 4*ceil(L/64) of block table + 8192 (q) + 256 (weights) + 4
         (seq_len) + 8192 (output); rows with L <= 2048 move only the block
-        table, seq_len and output.  Logit scratch is not counted."""
+        table, seq_len and output.  With rows_per_seq > 1 a group of rows
+        that shares a sequence reads its index-K and block table once, for
+        its longest row (132*Lmax + 4*ceil(Lmax/64)), when any of its rows is
+        scored; q, weights, seq_len and output stay per row.  Logit scratch is
+        not counted."""
         sl = self.seq_lens.cpu().numpy().astype(np.int64)
         sl = np.clip(sl, 0, self.max_pages * PAGE_SIZE)
         pages = (sl + PAGE_SIZE - 1) // PAGE_SIZE
         scored = sl > TOPK
-        per = np.where(scored, 132 * sl + 8192 + 256, 0) + 4 * pages + 4 + 4 * TOPK
-        return int(per.sum())
+        R = max(1, self.rows_per_seq)
+        if R == 1:
+            per = np.where(scored, 132 * sl + 8192 + 256, 0) + 4 * pages + 4 + 4 * TOPK
+            return int(per.sum())
+        lmax = sl.reshape(-1, R).max(axis=1)
+        g_scored = lmax > TOPK
+        shared = np.where(g_scored, 132 * lmax, 0) + 4 * ((lmax + PAGE_SIZE - 1) // PAGE_SIZE)
+        per_row = np.where(np.repeat(g_scored, R), 8192 + 256, 0) + 4 + 4 * TOPK
+        return int(shared.sum() + per_row.sum())
 
     def scored_tokens(self) -> int:
         sl = self.seq_lens.cpu().numpy().astype(np.int64)
@@ -146,7 +158,7 @@ def make_inputs(seq_lens, *, max_pages: int | None = None, pool_pages: int | Non
         k_cache[p0:p1] = pack_pages(kq, sc)
     return Inputs(q, k_cache, weights.contiguous(),
                   torch.from_numpy(sl.astype(np.int32)).to(device),
-                  torch.from_numpy(bt).to(device), name=name, seed=seed)
+                  torch.from_numpy(bt).to(device), name=name, seed=seed, rows_per_seq=share_rows)
 
 
 def plant_tokens(inp: Inputs, row: int, tokens, boost: float = 4.0) -> None:

@@ -79,6 +79,15 @@ typedef struct dsai_args {
   int32_t num_pages;
   int32_t flags;             /* DSAI_FLAG_*                                            */
   void* ev_after_score;      /* optional cudaEvent_t recorded after the scoring launch */
+  int32_t rows_per_seq;      /* 0 or 1: rows independent.  2-4: consecutive groups of
+                                that many rows are query tokens of one sequence (multi-
+                                query decode, next-n / MTP, causal prefill rows): they
+                                must agree on block_table over every page each of them
+                                reaches, and each group's K pages are read once, through
+                                the block_table row of its longest row.  rows must be a
+                                multiple of it.  No counterpart in the reference, whose
+                                rows are always scored one by one
+                                (solution/python/kernel.cu:1208-1479).              */
 } dsai_args;
 
 /* Bytes of device workspace dsai_run needs for these sizes (256-B aligned

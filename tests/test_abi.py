@@ -75,6 +75,34 @@ def test_run_rejects_bad_arguments_without_device(dsai_lib):
     assert dsai_lib.dsai_run(ctypes.byref(a), 256, 1 << 20, None) == -1
 
 
+def test_rows_per_seq_checked_without_device(dsai_lib):
+    for rows, rps in ((3, 2), (8, 5), (8, -1)):
+        a = _args(rows=rows, max_pages=4, num_pages=4, seq_lens=16, block_table=32, topk_indices=64,
+                  rows_per_seq=rps)
+        assert dsai_lib.dsai_run(ctypes.byref(a), 256, 1 << 20, None) == _lib.E_INVALID
+        assert b"rows_per_seq" in dsai_lib.dsai_last_error()
+
+
+def test_args_struct_layout_matches_header(tmp_path):
+    """The ctypes mirror of dsai_args has the C struct's size and offsets."""
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in _lib.DsaiArgs._fields_]
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "dsai.h"', "int main(void) {"]
+    lines += [f'  printf("%zu\\n", offsetof(dsai_args, {f}));' for f in fields]
+    lines += ['  printf("%zu\\n", sizeof(dsai_args));', "  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(_lib.DsaiArgs, f).offset for f in fields] + [ctypes.sizeof(_lib.DsaiArgs)]
+    assert got == want
+
+
 def test_merge_and_status_reject_null(dsai_lib):
     assert dsai_lib.dsai_merge_pairs(None, None, -1, None, 4, None, None, None) == -1
     assert dsai_lib.dsai_merge_pairs(None, None, 4, 16, 4, 16, 16, None) == -1

@@ -19,7 +19,9 @@
 // rows is longer than the top-K (or every row is requested).
 //
 // One CTA per SM, 2 + 4R warps:
-//   warp 0      producer: K pages (TMA, 128-B swizzle) into an 8-stage ring,
+//   warp 0      producer: K pages (TMA, 128-B swizzle) into a ring of as many
+//               stages as shared memory holds (9-11: the bytes in flight per
+//               SM set the HBM rate this kernel reaches),
 //               scales into a 16-slot ring, and at a group change the R
 //               queries (R x 8 KB, stacked so they form one N = 64*R operand)
 //               and the R x 64 head weights (one bulk copy) into 2-slot rings.
@@ -28,9 +30,9 @@
 //   warps 2..   epilogue: one warp per (TMEM lane quadrant, group row), so
 //               4R warps share the issue slots and hide each other's
 //               latencies.  Weights are read from shared memory (broadcast),
-//               the head sum runs on packed f32x2 FMAs, and the stores and
-//               histogram reductions are those of the per-row scorer, with
-//               the row's own length.
+//               the head sum runs on packed f32x2 FMAs, and each token's
+//               logit is stored and reduced into its row's histogram (one
+//               reduction per token), with the row's own length.
 #include "common.cuh"
 #include "launch.h"
 #include "sm100.cuh"
@@ -42,10 +44,8 @@ namespace {
 using namespace sm100;
 
 constexpr int kMqMaxThreads = 64 + 128 * 4;
-constexpr int kMqStages = 8;
 constexpr int kMqScaleSlots = 16;
 constexpr int kMqTmemCols = 512;
-constexpr int kMqMaxGroups = kMaxRowsPerLaunch / 2;
 constexpr uint32_t kMqScaleTx = kPage * 4;
 
 template <int R>
@@ -54,6 +54,8 @@ struct MqTraits {
   static constexpr int kAccs = kMqTmemCols / kN >= 4 ? 4 : 2;
   static constexpr int kEpiWarps = 4 * R;                 // one per (lane quadrant, row)
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kStages = R == 2 ? 11 : (R == 3 ? 10 : 9);  // fill the shared memory
+  static constexpr int kMaxGroups = kMaxRowsPerLaunch / R;
   static_assert(R >= 2 && R <= 4, "2 to 4 rows per group");
   static_assert(kAccs * kN <= kMqTmemCols, "accumulators must fit TMEM");
 };
@@ -75,12 +77,12 @@ struct MqParams {
 
 template <int R>
 struct MqSmem {
-  uint8_t k[kMqStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
+  uint8_t k[MqTraits<R>::kStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
   uint8_t q[2][R * kQBytes];              // R stacked queries, SW128 K-major, N = 64R
   alignas(128) float w[2][R][kHeads];
   alignas(1024) float scale[kMqScaleSlots][kTileTok];
-  uint64_t full[kMqStages];
-  uint64_t empty[kMqStages];
+  uint64_t full[MqTraits<R>::kStages];
+  uint64_t empty[MqTraits<R>::kStages];
   uint64_t sfull[kMqScaleSlots];
   uint64_t sempty[kMqScaleSlots];
   uint64_t qfull[2];
@@ -93,16 +95,17 @@ struct MqSmem {
   uint32_t tmem_base;
   int abort;
   int warp_sums[kMqMaxThreads / 32];
-  int gstart[kMqMaxGroups + 1];
-  int glead[kMqMaxGroups];  // row (within the launch) whose block-table row the group reads
-  int glen[kMqMaxGroups];   // the group's longest effective row length
+  int gstart[MqTraits<R>::kMaxGroups + 1];
+  int glead[MqTraits<R>::kMaxGroups];  // row (within the launch) whose block-table row the group reads
+  int glen[MqTraits<R>::kMaxGroups];   // the group's longest effective row length
 };
 
 template <int R>
 constexpr int mq_smem_bytes() {
   return static_cast<int>(sizeof(MqSmem<R>)) + 1024;
 }
-static_assert(mq_smem_bytes<4>() <= 232448, "the group scorer must fit one SM's shared memory");
+static_assert(mq_smem_bytes<2>() <= 232448 && mq_smem_bytes<3>() <= 232448 && mq_smem_bytes<4>() <= 232448,
+              "the group scorer must fit one SM's shared memory");
 
 template <int R>
 __device__ __forceinline__ void mq_fail(MqSmem<R>& s, int* status) {
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(MqTraits<R>::kThreads, 1)
     score_mq_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_s, const MqParams p) {
   using Tr = MqTraits<R>;
-  constexpr int kN = Tr::kN, kAccs = Tr::kAccs, kEpiWarps = Tr::kEpiWarps;
+  constexpr int kN = Tr::kN, kAccs = Tr::kAccs, kEpiWarps = Tr::kEpiWarps, kMqStages = Tr::kStages;
   constexpr bool kSplitLoad = Tr::kThreads > 448;  // fewer than 128 registers a thread
   extern __shared__ uint8_t smem_raw[];
   MqSmem<R>& s = *reinterpret_cast<MqSmem<R>*>(
@@ -453,14 +456,11 @@ __global__ void __launch_bounds__(MqTraits<R>::kThreads, 1)
         const bool live = t_abs < L;
         if (live) p.logits[b * p.ld + t_abs] = logit;
         if (L > kTopK) {
-          // lanes sharing a bin add once (see the per-row scorer)
+          // One reduction per token: with 4R epilogue warps sharing the issue
+          // slots, aggregating equal bins in the warp first (the per-row
+          // scorer's match) costs more than the L2 reductions it saves.
           const uint32_t bin = ordered_key(logit) >> (32 - kHistBits);
-          const unsigned act = __ballot_sync(0xffffffffu, live);
-          if (live) {
-            const unsigned peers = __match_any_sync(act, bin);
-            if (lane == __ffs(peers) - 1)
-              atomicAdd(p.hist + b * kHistBins + bin, static_cast<uint32_t>(__popc(peers)));  // RED
-          }
+          if (live) atomicAdd(p.hist + b * kHistBins + bin, 1u);  // RED
         }
         if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
         if (++sslot == kMqScaleSlots) { sslot = 0; sphase ^= 1u; }
@@ -519,7 +519,7 @@ cudaError_t launch_mq(const ScoreLaunch& lp, const CUtensorMap& tq, const CUtens
 
 cudaError_t launch_score_groups(const ScoreLaunch& lp, int rows_per_group, const CUtensorMap& tmap_q,
                                 const CUtensorMap& tmap_k, const CUtensorMap& tmap_s, cudaStream_t stream) {
-  if (rows_per_group < 2 || lp.rows % rows_per_group != 0 || lp.rows / rows_per_group > kMqMaxGroups)
+  if (rows_per_group < 2 || lp.rows % rows_per_group != 0 || lp.rows > kMaxRowsPerLaunch)
     return cudaErrorInvalidValue;
   switch (rows_per_group) {
     case 2: return launch_mq<2>(lp, tmap_q, tmap_k, tmap_s, stream);

@@ -610,6 +610,7 @@ struct WideSmem {
 constexpr int kWideSmemBytes = static_cast<int>(sizeof(WideSmem));
 static_assert(kWideSmemBytes <= 232448, "the wide CTA must fit");
 static_assert(kBins2 == kWThreads && kHistBins == 4 * kWThreads, "bin ownership");
+static_assert(kSmall * 16 == kWThreads, "the final ranking uses 16 threads per key");
 
 // One 1024-thread CTA per row: no cross-CTA traffic, and no block-wide scan
 // in the pass (output and candidate slots come from one shared atomic per
@@ -620,7 +621,7 @@ template <bool kIds>
 __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectLaunch p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   WideSmem& s = *reinterpret_cast<WideSmem*>(smem_raw);
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x;
   const int b = blockIdx.x;
   // Before the wait on the scoring kernel: what does not depend on it.  This
   // kernel's predecessor in the stream is that scoring launch, which writes
@@ -839,27 +840,25 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
       }
     }
     __syncthreads();
-    if (tid < 32) {
-      // Rank the n2 keys (largest first, ties by list position); the k2 best
-      // take the last k2 slots.
+    {
+      // Rank the n2 keys (largest first, ties by list position) with the
+      // whole block: key i is compared with keys 4c..4c+3 by thread 16i + c
+      // and the 16 partial counts are summed over those lanes (one step of
+      // latency instead of a 32-step chain in one warp).  The k2 best take
+      // the last k2 slots.
       const int n = min(s.small_count, kSmall);
-      const uint32_t ka = lane < n ? s.small_key[lane] : 0u;
-      const uint32_t kb = lane + 32 < n ? s.small_key[lane + 32] : 0u;
-      int ra = 0, rb = 0;
-      for (int o = 0; o < 32; ++o) {
-        const uint32_t xa = __shfl_sync(0xffffffffu, ka, o);
-        const uint32_t xb = __shfl_sync(0xffffffffu, kb, o);
-        if (o < n) {
-          ra += (xa > ka || (xa == ka && o < lane)) ? 1 : 0;
-          rb += (xa > kb || (xa == kb && o < lane + 32)) ? 1 : 0;
-        }
-        if (o + 32 < n) {
-          ra += (xb > ka || (xb == ka && o + 32 < lane)) ? 1 : 0;
-          rb += (xb > kb || (xb == kb && o < lane)) ? 1 : 0;
-        }
+      const int i = tid >> 4, c = tid & 15;
+      const uint32_t ki = i < n ? s.small_key[i] : 0u;
+      int r = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = 4 * c + q;
+        const uint32_t kj = j < n ? s.small_key[j] : 0u;
+        r += (j < n && (kj > ki || (kj == ki && j < i))) ? 1 : 0;
       }
-      if (lane < n && ra < k2) out.emit(kTopK - k2 + ra, s.small_val[lane], ka);
-      if (lane + 32 < n && rb < k2) out.emit(kTopK - k2 + rb, s.small_val[lane + 32], kb);
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+      if (c == 0 && i < n && r < k2) out.emit(kTopK - k2 + r, s.small_val[i], ki);
     }
     return;
   }

@@ -24,6 +24,8 @@ cpu_baseline: the CPU oracle (exact C restatement, all host threads) on a
            the host cores, each step a bounded sample of the workload.
 --op write_k: the index-K cache writer (bf16 keys -> e4m3 pages) on
            --tokens new tokens per call instead of the indexer.
+--op prefill: one prefill chunk (--chunk causal rows of a --last-len
+           sequence), in groups of 4 rows and row by row.
 --op graph: small-batch latency (config 0), kernel(...) called eagerly
            against the same call replayed from a CUDA graph (IndexerGraph).
 """
@@ -623,6 +625,56 @@ def bench_graph(args, world, rank, local):
     }
 
 
+def bench_prefill(args, world, rank, local):
+    """A prefill chunk: `--chunk` causal query rows of one sequence whose
+    last row sees `--last-len` tokens, all over the sequence's block table.
+    Timed in groups of 4 rows (rows_per_seq=4: each K tile staged once per
+    group) and row by row, each call bracketed by CUDA events, with L2
+    flushed (a 256 MB write) before every call since the chunk's K pages
+    (~8.6 MB for 64K tokens) would otherwise stay in L2."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = W.prefill_inputs(args.chunk, args.last_len, device=dev)
+    out = g.out()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    token_rows = int(g.seq_lens.to(torch.int64).sum().item())
+    alg = g.algorithmic_bytes()  # K once per chunk would be the floor; counted per group of 4 here
+
+    def timed(rps):
+        for _ in range(args.warmup):
+            run(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out, rows_per_seq=rps)
+        torch.cuda.synchronize()
+        total = 0.0
+        for _ in range(args.steps):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            run(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out, rows_per_seq=rps)
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+        return total / args.steps * 1e3
+
+    clocks = ClockSampler(dev)
+    clocks.start()
+    us4 = timed(4)
+    clk = clocks.stop()
+    us1 = timed(1)
+    return {
+        "metric": f"us per prefill-chunk indexer call ({args.chunk} causal rows, last row {args.last_len} tokens)",
+        "value": round(us4, 2), "unit": "us", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(us4 / 1e3, 5), "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> f32 (scores), u32 keys (select)", "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": g.name, "rows": g.rows, "rows_per_seq": 4, "max_pages": g.max_pages,
+                   "l2": "256 MB write before every timed call"},
+        "token_rows_per_s": round(token_rows / (us4 / 1e6), 1),
+        "algorithmic_bytes": alg,
+        "row_by_row_us": round(us1, 2),
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -636,7 +688,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")
     ap.add_argument("--ref-step-budget", type=float, default=2.0, help="seconds per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k", "graph"],
+    ap.add_argument("--chunk", type=int, default=256, help="--op prefill: query rows of the chunk")
+    ap.add_argument("--last-len", type=int, default=65536, help="--op prefill: tokens the last row sees")
+    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k", "graph", "prefill"],
                     help="write_k: the index-K cache writer; graph: small-batch latency, eager vs CUDA graph")
     ap.add_argument("--tokens", type=int, default=131072, help="new tokens per write_k call")
     args = ap.parse_args()
@@ -648,6 +702,8 @@ def main():
             line = bench_writer(args, world, rank, local) if rank == 0 else None
         elif args.op == "graph":
             line = bench_graph(args, world, rank, local) if rank == 0 else None
+        elif args.op == "prefill":
+            line = bench_prefill(args, world, rank, local) if rank == 0 else None
         elif args.impl == "reference":
             line = bench_reference(args, world, rank)
         elif args.config == 3:

@@ -194,6 +194,18 @@ CONFIGS = {
 }
 
 
+def prefill_inputs(chunk: int, last_len: int, *, seed: int = 7, device="cpu", rows_per_seq: int = 4) -> Inputs:
+    """The indexer rows of one prefill chunk: `chunk` query tokens of one
+    sequence at positions last_len - chunk .. last_len - 1, so row i sees the
+    causal prefix of length last_len - chunk + 1 + i; every row holds the
+    sequence's block-table row.  The kernel scores them in groups of
+    `rows_per_seq` consecutive rows (each group reads the K pages once)."""
+    sl = np.arange(last_len - chunk + 1, last_len + 1)
+    inp = make_inputs(sl, seed=seed, device=device, name=f"prefill{chunk}x{last_len}", share_rows=chunk)
+    inp.rows_per_seq = rows_per_seq
+    return inp
+
+
 def config_inputs(config: int, *, seed: int | None = None, device="cpu", rows: int | None = None) -> Inputs:
     """Inputs of one benchmark configuration (`rows` shrinks the batch for a
     quick case of the same distribution)."""

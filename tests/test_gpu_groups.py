@@ -125,6 +125,22 @@ def test_groups_over_launch_limit():
     same_ids(ids_g, ids_r, lens)
 
 
+@pytest.mark.parametrize("chunk,last_len", [(32, 12000), (32, 2061)])
+def test_prefill_chunk(oracle_mod, chunk, last_len):
+    """A prefill chunk (causal rows of one sequence over one block table) in
+    groups of 4; the second chunk crosses 2048, so its first groups mix rows
+    that are all selected with scored rows."""
+    inp = W.prefill_inputs(chunk, last_len, seed=64)
+    g = inp.to(DEV)
+    lens = inp.seq_lens.numpy()
+    ids_g, lg_g, st = gpu_run(g, 4)
+    ids_r, lg_r, _ = gpu_run(g, 1)
+    assert st == 0
+    same_logits(lg_g, lg_r, lens)
+    same_ids(ids_g, ids_r, lens)
+    check(oracle_mod, inp, ids_g, lg_g, rows=[0, 5, 17, chunk - 1])
+
+
 def test_group_arguments_rejected():
     inp = W.make_inputs([3000, 3000, 3000], seed=63).to(DEV)
     out = inp.out()

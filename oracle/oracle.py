@@ -271,3 +271,49 @@ def check_logits(gpu_logits, ora_logits, mag, seq_lens, rtol=1e-2, mag_tol=1e-4)
         if L:
             worst = max(worst, float((err / (np.abs(o) + m + 1e-30)).max()))
     return worst
+
+
+# ---------------------------------------------------------------- sparse MLA attention
+# The consumer of the indexer's output (the contest operator
+# dsa_sparse_attention_h16_ckv512_kpe64_topk2048_ps64, which lives in a
+# repository not mounted here).  Restated from the published definition of
+# that operator in flashinfer 0.6.11.post2 (flashinfer/trace/templates/
+# attention.py, `_dsa_paged_reference` / `dsa_paged_trace`); pinned by the
+# golden vectors in tests/golden/sparse_attn_golden.npz that
+# tests/golden/make_sparse_attn_golden.py generated from that reference:
+#   for each query token t and head h, over the valid entries i of
+#   sparse_indices[t] (flat slot ids page*64 + slot; -1 = padding):
+#     s_i   = (q_nope[t,h] . ckv[i] + q_pe[t,h] . kpe[i]) * sm_scale
+#     out   = sum_i softmax(s)_i * ckv[i]          (bf16 on the device)
+#     lse   = log2(sum_i exp(s_i))                 (base 2, fp32)
+#   a token with no valid entry gives out = 0 and lse = -inf.
+
+
+def sparse_attention(q_nope, q_pe, ckv, kpe, sparse_indices, sm_scale):
+    """fp64 restatement; inputs are float arrays (bf16 values widened),
+    ckv [num_pages, 64, 512], kpe [num_pages, 64, 64].  Returns (out fp64
+    [T, H, 512], lse fp64 [T, H])."""
+    q_nope = np.asarray(q_nope, np.float64)
+    q_pe = np.asarray(q_pe, np.float64)
+    kc = np.asarray(ckv, np.float64).reshape(-1, q_nope.shape[-1])
+    kp = np.asarray(kpe, np.float64).reshape(-1, q_pe.shape[-1])
+    T, H, D = q_nope.shape
+    out = np.zeros((T, H, D), np.float64)
+    lse = np.full((T, H), -np.inf, np.float64)
+    for t in range(T):
+        ids = np.asarray(sparse_indices[t]).astype(np.int64)
+        ids = ids[ids != -1]
+        if ids.size == 0:
+            continue
+        s = (q_nope[t] @ kc[ids].T + q_pe[t] @ kp[ids].T) * float(sm_scale)  # [H, n]
+        m = s.max(axis=1, keepdims=True)
+        e = np.exp(s - m)
+        z = e.sum(axis=1, keepdims=True)
+        out[t] = (e / z) @ kc[ids]
+        lse[t] = (m[:, 0] + np.log(z[:, 0])) / np.log(2.0)
+    return out, lse
+
+
+def bf16_to_float(u16: np.ndarray) -> np.ndarray:
+    """bfloat16 bit patterns (uint16) -> float32."""
+    return (np.asarray(u16, np.uint16).astype(np.uint32) << 16).view(np.float32)

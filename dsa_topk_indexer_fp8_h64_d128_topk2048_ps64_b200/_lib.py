@@ -25,6 +25,10 @@ DSAI_OK = 0
 STATUS_SEQLEN_CLAMPED = 0x1
 STATUS_BAD_PAGE = 0x2
 STATUS_WAIT_TIMEOUT = 0x4
+STATUS_BAD_INDEX = 0x8
+ATTN_HEADS = 16
+ATTN_CKV_DIM = 512
+ATTN_KPE_DIM = 64
 FLAG_SCORE_ALL_ROWS = 0x1
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
@@ -37,6 +41,7 @@ EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
     "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
     "dsai_run_noalloc", "dsai_selftest_wait_timeout", "dsai_write_k",
+    "dsai_sparse_attn_workspace_size", "dsai_sparse_attn",
 )
 
 
@@ -56,6 +61,22 @@ class DsaiArgs(ctypes.Structure):
         ("flags", ctypes.c_int32),
         ("ev_after_score", ctypes.c_void_p),
         ("rows_per_seq", ctypes.c_int32),
+    ]
+
+
+class DsaiAttnArgs(ctypes.Structure):
+    """Mirror of ``dsai_attn_args`` in include/dsai.h."""
+    _fields_ = [
+        ("q_nope", ctypes.c_void_p),
+        ("q_pe", ctypes.c_void_p),
+        ("ckv_cache", ctypes.c_void_p),
+        ("kpe_cache", ctypes.c_void_p),
+        ("sparse_indices", ctypes.c_void_p),
+        ("output", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("sm_scale", ctypes.c_float),
+        ("num_tokens", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
     ]
 
 
@@ -92,6 +113,10 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.dsai_selftest_wait_timeout.restype = ctypes.c_int
         lib.dsai_write_k.argtypes = [vp, i32, vp, i32, vp, i32, vp]
         lib.dsai_write_k.restype = ctypes.c_int
+        lib.dsai_sparse_attn_workspace_size.argtypes = [i32]
+        lib.dsai_sparse_attn_workspace_size.restype = sz
+        lib.dsai_sparse_attn.argtypes = [ctypes.POINTER(DsaiAttnArgs), vp, sz, vp]
+        lib.dsai_sparse_attn.restype = ctypes.c_int
         lib.dsai_read_status.argtypes = [vp, vp, ctypes.POINTER(i32)]
         lib.dsai_read_status.restype = ctypes.c_int
         lib.dsai_last_error.argtypes = []

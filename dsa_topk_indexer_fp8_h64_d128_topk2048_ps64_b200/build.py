@@ -16,7 +16,7 @@ PKG_DIR = Path(__file__).resolve().parent
 REPO = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libdsai.so"
-SOURCES = ["score.cu", "score_mq.cu", "select.cu", "api.cu", "noalloc.cu", "writer.cu"]
+SOURCES = ["score.cu", "score_mq.cu", "select.cu", "api.cu", "noalloc.cu", "writer.cu", "attn.cu"]
 HEADERS = ["common.cuh", "sm100.cuh", "launch.h", "tiles.cuh"]
 
 NVCC_FLAGS = [

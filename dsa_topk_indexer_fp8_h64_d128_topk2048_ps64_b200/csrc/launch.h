@@ -36,6 +36,27 @@ cudaError_t launch_score(const ScoreLaunch& p, const CUtensorMap& tmap_q, const 
 cudaError_t launch_score_groups(const ScoreLaunch& p, int rows_per_group, const CUtensorMap& tmap_q,
                                 const CUtensorMap& tmap_k, const CUtensorMap& tmap_s, cudaStream_t stream);
 
+struct AttnLaunch {
+  const void* q_nope;
+  const void* q_pe;
+  const void* ckv;
+  const void* kpe;
+  const int32_t* idx;
+  void* out;
+  float* lse;
+  void* workspace;   // 256-B status header, then the split partials
+  float sm_scale;
+  int num_tokens;
+  int num_slots;
+};
+
+// Sparse MLA attention (attn.cu): splits per token and workspace bytes for
+// the current device, and the launch (attention kernel, then the combine
+// kernel when a token is split).
+int attn_splits(int num_tokens);
+size_t attn_workspace_bytes(int num_tokens);
+cudaError_t launch_attn(const AttnLaunch& a, cudaStream_t stream);
+
 struct SelectLaunch {
   const float* logits;  // [rows, ld]
   int ld;

@@ -19,7 +19,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status", "write_index_k", "IndexerGraph"]
+__all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status", "write_index_k", "IndexerGraph",
+           "sparse_attention", "read_attn_status"]
 
 _FP8 = getattr(torch, "float8_e4m3fn", None)
 
@@ -193,6 +194,77 @@ def write_index_k(k_new: torch.Tensor, slot_ids: torch.Tensor, k_index_cache_fp8
                                     k_index_cache_fp8.data_ptr(),
                                     int(k_index_cache_fp8.numel() // _lib.PAGE_BYTES),
                                     torch.cuda.current_stream(dev).cuda_stream))
+
+
+_attn_ws: dict = {}
+
+
+def _attn_workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
+    """Per-device workspace of the sparse attention (status header zeroed
+    once at allocation; grown when a call needs more)."""
+    ws = _attn_ws.get(dev)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        _attn_ws[dev] = ws
+    return ws
+
+
+def sparse_attention(q_nope: torch.Tensor, q_pe: torch.Tensor, ckv_cache: torch.Tensor, kpe_cache: torch.Tensor,
+                     sparse_indices: torch.Tensor, sm_scale: float, output: torch.Tensor, lse: torch.Tensor) -> None:
+    """Sparse MLA attention over the indexer's top-2048 slots (the operator
+    after the indexer in a DSA decode step), destination-passing: for token
+    t and head h over the entries of ``sparse_indices[t]`` that are not -1
+    (flat slot ids page*64 + slot), ``output[t, h]`` ([T, 16, 512] bf16)
+    gets softmax(scores * sm_scale) @ ckv and ``lse[t, h]`` ([T, 16] fp32)
+    the base-2 log-sum-exp of the scaled scores (0 and -inf for a token
+    with no valid entry).  q_nope [T, 16, 512], q_pe [T, 16, 64],
+    ckv_cache [num_pages, 64, 512] and kpe_cache [num_pages, 64, 64] are
+    bf16.  Runs on the current stream."""
+    bf = torch.bfloat16
+    for name, x in (("q_nope", q_nope), ("q_pe", q_pe), ("ckv_cache", ckv_cache), ("kpe_cache", kpe_cache),
+                    ("output", output)):
+        _req(x.is_cuda and x.is_contiguous() and x.dtype == bf, f"{name} must be bfloat16 contiguous CUDA")
+    _check_int32(sparse_indices, "sparse_indices")
+    _req(lse.is_cuda and lse.is_contiguous() and lse.dtype == torch.float32, "lse must be float32 contiguous CUDA")
+    T = int(q_nope.size(0)) if q_nope.dim() == 3 else -1
+    H, D, DP = _lib.ATTN_HEADS, _lib.ATTN_CKV_DIM, _lib.ATTN_KPE_DIM
+    _req(q_nope.dim() == 3 and tuple(q_nope.shape[1:]) == (H, D), "q_nope shape must be [T, 16, 512]")
+    _req(tuple(q_pe.shape) == (T, H, DP), "q_pe shape must be [T, 16, 64]")
+    _req(ckv_cache.dim() == 3 and tuple(ckv_cache.shape[1:]) == (_lib.PAGE_SIZE, D),
+         "ckv_cache shape must be [num_pages, 64, 512]")
+    num_pages = int(ckv_cache.size(0))
+    _req(tuple(kpe_cache.shape) == (num_pages, _lib.PAGE_SIZE, DP), "kpe_cache shape must be [num_pages, 64, 64]")
+    _req(tuple(sparse_indices.shape) == (T, _lib.TOPK), "sparse_indices shape must be [T, 2048]")
+    _req(tuple(output.shape) == (T, H, D) and tuple(lse.shape) == (T, H), "output / lse shapes must be [T, 16, 512] / [T, 16]")
+    if T == 0:
+        return
+    lib = _lib.load_library()
+    dev = q_nope.device
+    with torch.cuda.device(dev):
+        ws = _attn_workspace(dev, int(lib.dsai_sparse_attn_workspace_size(T)))
+        a = _lib.DsaiAttnArgs()
+        a.q_nope, a.q_pe = q_nope.data_ptr(), q_pe.data_ptr()
+        a.ckv_cache, a.kpe_cache = ckv_cache.data_ptr(), kpe_cache.data_ptr()
+        a.sparse_indices = sparse_indices.data_ptr()
+        a.output, a.lse = output.data_ptr(), lse.data_ptr()
+        a.sm_scale = float(sm_scale)
+        a.num_tokens, a.num_pages = T, num_pages
+        _lib.check(lib.dsai_sparse_attn(ctypes.byref(a), ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream(dev).cuda_stream))
+
+
+def read_attn_status(device=None) -> int:
+    """Returns and clears the status bits of the sparse attention's workspace
+    on `device` (synchronises its current stream)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    ws = _attn_ws.get(dev)
+    if ws is None:
+        return 0
+    lib = _lib.load_library()
+    v = ctypes.c_int32(0)
+    with torch.cuda.device(dev):
+        _lib.check(lib.dsai_read_status(ws.data_ptr(), torch.cuda.current_stream(dev).cuda_stream, ctypes.byref(v)))
+    return int(v.value)
 
 
 def read_status(device=None) -> int:

@@ -42,6 +42,9 @@ extern "C" {
 #define DSAI_HEAD_DIM 128
 #define DSAI_PAGE_SIZE 64
 #define DSAI_TOPK 2048
+#define DSAI_ATTN_HEADS 16     /* sparse MLA attention: query heads */
+#define DSAI_ATTN_CKV_DIM 512  /* compressed KV (latent) dimension */
+#define DSAI_ATTN_KPE_DIM 64   /* rotary key dimension */
 #define DSAI_PAGE_BYTES 8448
 #define DSAI_SCALE_OFFSET 8192
 
@@ -62,6 +65,7 @@ extern "C" {
 #define DSAI_STATUS_SEQLEN_CLAMPED 0x1 /* a seq_len was < 0 or > max_pages*64 */
 #define DSAI_STATUS_BAD_PAGE 0x2       /* a block_table entry was outside [0, num_pages) */
 #define DSAI_STATUS_WAIT_TIMEOUT 0x4   /* a bounded on-chip wait gave up */
+#define DSAI_STATUS_BAD_INDEX 0x8      /* sparse attention: a sparse index outside [-1, num_pages*64) */
 
 /* Flags for dsai_args.flags. */
 #define DSAI_FLAG_SCORE_ALL_ROWS 0x1 /* also score rows with seq_len <= 2048 (debug logits) */
@@ -156,6 +160,42 @@ DSAI_API int dsai_write_k(const void* k_new, int32_t dtype, const int32_t* slot_
 /* Copy the workspace status word to *status_out (host), then clear it.
  * Synchronises `stream`. */
 DSAI_API int dsai_read_status(void* workspace, void* stream, int32_t* status_out);
+
+/* Sparse MLA attention over the indexer's output: the operator after the
+ * indexer in a DSA decode step (dsa_sparse_attention_h16_ckv512_kpe64_
+ * topk2048_ps64).  No counterpart in this reference, which names it as the
+ * next stage (final_writeup.md:27-41); its published definition is
+ * flashinfer 0.6.11.post2 `_dsa_paged_reference`.  For token t and head h,
+ * over the entries i of sparse_indices[t] that are not -1 (flat slot ids
+ * page*64 + slot, as dsai_run writes them):
+ *   s_i = (q_nope[t,h] . ckv[i] + q_pe[t,h] . kpe[i]) * sm_scale
+ *   output[t,h] = sum_i softmax(s)_i ckv[i]   (bf16)
+ *   lse[t,h]    = log2(sum_i exp(s_i))        (fp32; -inf, with output 0,
+ *                                              when no entry is valid)
+ * Indices outside [0, num_pages*64) other than -1 count as padding and set
+ * DSAI_STATUS_BAD_INDEX in the workspace status word. */
+typedef struct dsai_attn_args {
+  const void* q_nope;            /* [T, 16, 512] bf16                          */
+  const void* q_pe;              /* [T, 16, 64] bf16                           */
+  const void* ckv_cache;         /* [num_pages, 64, 512] bf16                  */
+  const void* kpe_cache;         /* [num_pages, 64, 64] bf16                   */
+  const int32_t* sparse_indices; /* [T, 2048] int32                            */
+  void* output;                  /* [T, 16, 512] bf16, written                 */
+  float* lse;                    /* [T, 16] fp32 (base 2), written             */
+  float sm_scale;
+  int32_t num_tokens;            /* T (at most 65535)                          */
+  int32_t num_pages;
+} dsai_attn_args;
+
+/* Bytes of workspace dsai_sparse_attn needs for num_tokens on the current
+ * device (256-B header with the status word, plus the per-split partial
+ * results when tokens are split across CTAs).  Zero the header once after
+ * allocating; the status word is sticky until dsai_read_status. */
+DSAI_API size_t dsai_sparse_attn_workspace_size(int32_t num_tokens);
+
+/* The sparse attention, destination-passing, on `stream`. */
+DSAI_API int dsai_sparse_attn(const dsai_attn_args* args, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 /* Self-test of failure detection: launches one kernel that waits on an
  * on-chip barrier nothing will complete, bounded by timeout_ns (at most 1 s);

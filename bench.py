@@ -26,6 +26,7 @@ cpu_baseline: the CPU oracle (exact C restatement, all host threads) on a
            --tokens new tokens per call instead of the indexer.
 --op prefill: one prefill chunk (--chunk causal rows of a --last-len
            sequence), in groups of 4 rows and row by row.
+--op attn: the sparse MLA attention that consumes the indexer's output.
 --op graph: small-batch latency (config 0), kernel(...) called eagerly
            against the same call replayed from a CUDA graph (IndexerGraph).
 """
@@ -33,6 +34,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -625,6 +627,80 @@ def bench_graph(args, world, rank, local):
     }
 
 
+def bench_attn(args, world, rank, local):
+    """Sparse MLA attention over top-2048 slots (the indexer's consumer):
+    --tokens-attn decode tokens, each over 2048 random slots of its own
+    4096-slot (64-page) range of a bf16 ckv/kpe pool (295 MB at 64 tokens,
+    larger than L2), two rotating index sets.  value = algorithmic bytes
+    (2048 x 1152 B of gathered rows + q, indices, output, lse per token) per
+    second over K back-to-back calls."""
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import sparse_attention
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    T = args.tokens_attn
+    pages = 64 * T
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    qn = torch.randn((T, 16, 512), generator=g, device=dev).to(torch.bfloat16)
+    qp = torch.randn((T, 16, 64), generator=g, device=dev).to(torch.bfloat16)
+    ckv = torch.randn((pages, 64, 512), generator=g, device=dev).to(torch.bfloat16)
+    kpe = torch.randn((pages, 64, 64), generator=g, device=dev).to(torch.bfloat16)
+    base = (torch.arange(T, device=dev, dtype=torch.int32) * 4096)[:, None]
+    idx_sets = [(torch.argsort(torch.rand((T, 4096), generator=g, device=dev), dim=1)[:, :2048].to(torch.int32) + base)
+                .contiguous() for _ in range(2)]
+    out = torch.empty((T, 16, 512), dtype=torch.bfloat16, device=dev)
+    lse = torch.empty((T, 16), dtype=torch.float32, device=dev)
+    scale = 1.0 / math.sqrt(192.0)
+    alg = T * (2048 * (1024 + 128) + 16 * 576 * 2 + 2048 * 4 + 16 * 512 * 2 + 16 * 4)
+    flops = T * 16 * 2048 * (576 + 512) * 2
+
+    def step(i):
+        sparse_attention(qn, qp, ckv, kpe, idx_sets[i % 2], scale, out, lse)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    peak, peak_src = measured_hbm_peak()
+    gbs = alg / (us / 1e6) / 1e9
+    line = {
+        "metric": f"sparse MLA attention GB/s (T={T} decode tokens x 2048 slots, h16 ckv512 kpe64)",
+        "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(us / 1e3, 5), "us_per_call": round(us, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 x bf16 -> f32 (tcgen05), bf16 out",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": f"attn: {T} tokens, 2048 of 4096 own slots each, {pages}-page bf16 pool",
+                   "l2": f"pool {(ckv.numel() + kpe.numel()) * 2 / 1e6:.0f} MB (> 126 MB L2), 2 rotating index sets"},
+        "roofline": {"kernel": "attn_kernel (+ attn_combine_kernel)", "bound": "hbm", "achieved": round(gbs, 1),
+                     "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(gbs / peak, 4),
+                     "algorithmic_bytes_per_launch": alg, "traffic": None,
+                     "tensor": {"achieved": round(flops / (us / 1e6) / 1e12, 1), "unit": "TFLOP/s",
+                                "algorithmic_flops_per_launch": flops}},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline:
+        from oracle import oracle  # CPU baseline leg only
+        n = 4
+        t0 = time.perf_counter()
+        oracle.sparse_attention(qn[:n].float().cpu().numpy(), qp[:n].float().cpu().numpy(),
+                                ckv.float().cpu().numpy(), kpe.float().cpu().numpy(),
+                                idx_sets[0][:n].cpu().numpy(), scale)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(alg / T * n / dt / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": f"{n} of {T} tokens (numpy fp64 oracle), {dt:.2f} s"}
+    return line
+
+
 def bench_prefill(args, world, rank, local):
     """A prefill chunk: `--chunk` causal query rows of one sequence whose
     last row sees `--last-len` tokens, all over the sequence's block table.
@@ -690,7 +766,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--chunk", type=int, default=256, help="--op prefill: query rows of the chunk")
     ap.add_argument("--last-len", type=int, default=65536, help="--op prefill: tokens the last row sees")
-    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k", "graph", "prefill"],
+    ap.add_argument("--tokens-attn", type=int, default=64, help="--op attn: decode tokens per call")
+    ap.add_argument("--op", default="indexer", choices=["indexer", "write_k", "graph", "prefill", "attn"],
                     help="write_k: the index-K cache writer; graph: small-batch latency, eager vs CUDA graph")
     ap.add_argument("--tokens", type=int, default=131072, help="new tokens per write_k call")
     args = ap.parse_args()
@@ -704,6 +781,8 @@ def main():
             line = bench_graph(args, world, rank, local) if rank == 0 else None
         elif args.op == "prefill":
             line = bench_prefill(args, world, rank, local) if rank == 0 else None
+        elif args.op == "attn":
+            line = bench_attn(args, world, rank, local) if rank == 0 else None
         elif args.impl == "reference":
             line = bench_reference(args, world, rank)
         elif args.config == 3:

@@ -18,12 +18,18 @@
 //              buffer (two buffers); -1 and out-of-range slots zero-fill.
 //   warp 8     MMA issuer: S^T = K Q^T (tcgen05 kind::f16 M128 N16 K16, bf16
 //              -> f32 in TMEM; rows 64-127 of the M = 128 operand are not
-//              used), then O^T += V^T P with the same buffer read MN-major
-//              (64 ckv dims x 8 rows per 128-B atom) as the A operand.
+//              used) as four independent accumulator chains over the 36
+//              K-steps (a single chain waits ~100 cycles per MMA on its
+//              accumulator), then O^T += V^T P with the same buffer read
+//              MN-major (64 ckv dims x 8 rows per 128-B atom) as the A operand.
 //   warps 4-7  online softmax in base 2 (warps 4-5 own the 64 rows), P in
-//              bf16 to shared memory, rescale of O^T in TMEM when the running
-//              maximum grows, and at the end out = O / l, lse = m + log2 l
-//              (or the split's (m, l, O) for the combine kernel).
+//              bf16 to shared memory, and at the end out = O / l,
+//              lse = m + log2 l (or the split's (m, l, O) for the combine
+//              kernel).  The reference maximum m moves only when a tile's
+//              maximum exceeds it by more than 8 (then O^T in TMEM is
+//              rescaled): probabilities stay <= 2^8, exact after the final
+//              division, and the rescale, which must wait for the previous
+//              tile's V^T P, is rare after the first tile.
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -50,10 +56,12 @@ constexpr int kAQBlockBytes = kAHeads * 128;             // 2 KB
 constexpr int kAQBytes = kAKBlocks * kAQBlockBytes;      // 18 KB
 constexpr int kAPBytes = kAHeads * kATile * 2;           // 2 KB
 constexpr int kAThreads = 288;
-constexpr int kATmemCols = 128;  // S: 2 x 16 columns, O^T: 4 x 16 columns from column 32
-constexpr int kAOCol = 32;
+constexpr int kASChains = 4;     // partial score accumulators per tile
+constexpr int kATmemCols = 256;  // S: 2 slots x 4 chains x 16 columns, O^T: 4 x 16 columns from column 128
+constexpr int kAOCol = 2 * kASChains * kAHeads;
 constexpr int kAMaxSplits = kATopK / kATile;  // 32
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // the reference maximum lags the true one by at most this
 
 struct AttnParams {
   const uint8_t* q_nope;  // [T, 16, 512] bf16
@@ -100,6 +108,62 @@ static_assert(kAKBlocks * kABlockBytes + kABlockBytes <= kABufBytes + kAQBytes,
 __device__ __forceinline__ void attn_fail(AttnSmem& s, int* status) {
   report(status, DSAI_STATUS_WAIT_TIMEOUT);
   *reinterpret_cast<volatile int*>(&s.abort) = 1;
+}
+
+// Reduces 16 per-lane values (one per head) over the 32 lanes of a warp by
+// halving: at each step a lane keeps half of its values, sends the other
+// half to its partner and combines, so 16 shuffles replace 16 x 5.  On
+// return lane L holds the result for head 8*b4 + 4*b3 + 2*b2 + b1 (b =
+// the bits of L); lanes L and L^1 hold the same head.
+template <bool kMax>
+__device__ __forceinline__ float warp_reduce16(const float (&v)[kAHeads], int lane) {
+  float a[8];
+  {
+    const bool hi = lane & 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float send = hi ? v[j] : v[j + 8];
+      const float keep = hi ? v[j + 8] : v[j];
+      const float got = __shfl_xor_sync(0xffffffffu, send, 16);
+      a[j] = kMax ? fmaxf(keep, got) : keep + got;
+    }
+  }
+  float b[4];
+  {
+    const bool hi = lane & 8;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float send = hi ? a[j] : a[j + 4];
+      const float keep = hi ? a[j + 4] : a[j];
+      const float got = __shfl_xor_sync(0xffffffffu, send, 8);
+      b[j] = kMax ? fmaxf(keep, got) : keep + got;
+    }
+  }
+  float c[2];
+  {
+    const bool hi = lane & 4;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float send = hi ? b[j] : b[j + 2];
+      const float keep = hi ? b[j + 2] : b[j];
+      const float got = __shfl_xor_sync(0xffffffffu, send, 4);
+      c[j] = kMax ? fmaxf(keep, got) : keep + got;
+    }
+  }
+  float d;
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? c[0] : c[1];
+    const float keep = hi ? c[1] : c[0];
+    const float got = __shfl_xor_sync(0xffffffffu, send, 2);
+    d = kMax ? fmaxf(keep, got) : keep + got;
+  }
+  const float got = __shfl_xor_sync(0xffffffffu, d, 1);
+  return kMax ? fmaxf(d, got) : d + got;
+}
+
+__device__ __forceinline__ int reduce16_head(int lane) {
+  return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
 }
 
 // Byte offset of 16-B chunk `c` (0-7) of row `r` in a 128-B-swizzled atom
@@ -158,14 +222,16 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
     fence_proxy_async_smem();
     mbar_arrive(&s.qfull);
     const int r0 = warp * 16;  // this warp's 16 rows of each tile
+    int32_t next_id = lane < 16 && tiles > 0 ? idx_row[r0 + lane] : -1;  // one tile ahead
     for (int i = 0; i < tiles; ++i) {
       const int b = i & 1;
+      const int32_t my_id = next_id;
+      if (lane < 16 && i + 1 < tiles) next_id = idx_row[(i + 1) * kATile + r0 + lane];
       // The buffer is free once O^T += V^T P of the tile two back completed.
       if (!__all_sync(0xffffffffu, mbar_wait(&s.done[b], ((i >> 1) & 1) ^ 1u, &s.abort, kWaitTimeoutNs))) {
         if (lane == 0) attn_fail(s, p.status);
         break;
       }
-      const int32_t my_id = lane < 16 ? idx_row[i * kATile + r0 + lane] : -1;
       const bool my_ok = lane < 16 && my_id >= 0 && my_id < p.num_slots;
       if (lane < 16 && my_id != -1 && !my_ok) report(p.status, DSAI_STATUS_BAD_INDEX);
       uint8_t* bb = s.buf[b];
@@ -199,37 +265,57 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
         const int b = i & 1;
         if (!mbar_wait(&s.full[b], (i >> 1) & 1, &s.abort, kWaitTimeoutNs)) return false;
         tc_fence_after();
-        const uint32_t d = tbase + static_cast<uint32_t>(16 * (i & 1));
-#pragma unroll 1
-        for (int kb = 0; kb < kAKBlocks; ++kb) {
-#pragma unroll
-          for (int k16 = 0; k16 < 4; ++k16) {
-            const uint64_t a = make_sw128_kmajor_desc(smem_u32(s.buf[b] + kb * kABlockBytes + k16 * 32));
-            const uint64_t q = make_sw128_kmajor_desc(smem_u32(s.q + kb * kAQBlockBytes + k16 * 32));
-            umma_bf16(d, a, q, idesc_s, (kb | k16) != 0 ? 1u : 0u);
-          }
+        const uint32_t d = tbase + static_cast<uint32_t>(kASChains * kAHeads * (i & 1));
+        const uint64_t a0 = make_sw128_kmajor_desc(smem_u32(s.buf[b]));
+        const uint64_t q0 = make_sw128_kmajor_desc(smem_u32(s.q));
+        // K-step n (16 dims) goes to chain n % 4; descriptor start addresses
+        // advance in 16-B units
+#pragma unroll 4
+        for (int n = 0; n < kAKBlocks * 4; ++n) {
+          const int kb = n >> 2, k16 = n & 3;
+          const uint64_t a = a0 + static_cast<uint64_t>((kb * kABlockBytes + k16 * 32) >> 4);
+          const uint64_t q = q0 + static_cast<uint64_t>((kb * kAQBlockBytes + k16 * 32) >> 4);
+          umma_bf16(d + static_cast<uint32_t>(kAHeads * (n % kASChains)), a, q, idesc_s, n >= kASChains ? 1u : 0u);
         }
         umma_commit(&s.sfull[i & 1]);
         return true;
       };
       if (ok && tiles > 0) ok = issue_s(0);
+      int next_s = 1;  // the next tile whose scores are not issued yet
       for (int i = 0; i < tiles && ok; ++i) {
-        // the next tile's scores go first: they overlap this tile's softmax
-        if (i + 1 < tiles && !issue_s(i + 1)) { ok = false; break; }
-        if (!mbar_wait(&s.pfull[i & 1], (i >> 1) & 1, &s.abort, kWaitTimeoutNs)) { ok = false; break; }
+        // While this tile's probabilities are computed, issue the next
+        // tile's scores if its rows have landed (never wait for them here:
+        // this tile's V^T P frees the buffer the gather needs next).
+        const uint64_t t0 = global_timer_ns();
+        while (!mbar_try_wait(&s.pfull[i & 1], (i >> 1) & 1)) {
+          if (next_s == i + 1 && next_s < tiles && mbar_try_wait(&s.full[next_s & 1], (next_s >> 1) & 1)) {
+            if (!issue_s(next_s)) { ok = false; break; }
+            ++next_s;
+          }
+          if (*reinterpret_cast<volatile int*>(&s.abort) || global_timer_ns() - t0 > kWaitTimeoutNs) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
         tc_fence_after();
         const int b = i & 1;
+        const uint64_t v0 = make_sw128_mnmajor_desc(smem_u32(s.buf[b]), kABlockBytes);
+        const uint64_t p0 = make_sw128_kmajor_desc(smem_u32(s.p[b]));
 #pragma unroll
-        for (int mb = 0; mb < 4; ++mb) {      // 128 ckv dims = 2 k-blocks per M block
+        for (int j = 0; j < kATile / 16; ++j) {  // 16 entries per MMA; the 4 M blocks interleave
 #pragma unroll
-          for (int j = 0; j < kATile / 16; ++j) {  // 16 entries per MMA
-            const uint64_t a = make_sw128_mnmajor_desc(
-                smem_u32(s.buf[b] + (2 * mb) * kABlockBytes + j * 2048), kABlockBytes);
-            const uint64_t pd = make_sw128_kmajor_desc(smem_u32(s.p[b] + j * 32));
+          for (int mb = 0; mb < 4; ++mb) {       // 128 ckv dims = 2 k-blocks per M block
+            const uint64_t a = v0 + static_cast<uint64_t>(((2 * mb) * kABlockBytes + j * 2048) >> 4);
+            const uint64_t pd = p0 + static_cast<uint64_t>((j * 32) >> 4);
             umma_bf16(tbase + static_cast<uint32_t>(kAOCol + 16 * mb), a, pd, idesc_o, (i > 0 || j > 0) ? 1u : 0u);
           }
         }
         umma_commit(&s.done[b]);
+        if (next_s == i + 1 && next_s < tiles) {
+          if (!issue_s(next_s)) { ok = false; break; }
+          ++next_s;
+        }
       }
       if (!ok) attn_fail(s, p.status);
       umma_commit(&s.drain);
@@ -245,63 +331,72 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
     volatile int* fail_a = &s.fail_a;
     volatile int* fail_b = &s.fail_b;
     bool finished = true;
+    int32_t next_id = sm && tiles > 0 ? idx_row[row] : -1;  // one tile ahead
     for (int i = 0; i < tiles; ++i) {
       const int k = i & 1;
       // A: scaled scores of the tile's rows and the tile maximum per head
       float x[kAHeads];
       if (sm) {
-        const int32_t id = idx_row[i * kATile + row];
+        const int32_t id = next_id;
+        if (i + 1 < tiles) next_id = idx_row[(i + 1) * kATile + row];
         const bool ok = id >= 0 && id < p.num_slots;
         const bool got = __all_sync(0xffffffffu, mbar_wait(&s.sfull[k], (i >> 1) & 1, &s.abort, kWaitTimeoutNs));
         if (got) {
           tc_fence_after();
-          uint32_t r[16];
-          tmem_ld_32x32b_x16(tbase + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(16 * k), r);
-          tmem_wait_ld();
+          // the four partial sums, two chains at a time: (c0 + c1) + (c2 + c3)
+          const uint32_t ta = tbase + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(kASChains * kAHeads * k);
+          float half[kAHeads];
 #pragma unroll
-          for (int h = 0; h < kAHeads; ++h) x[h] = ok ? __uint_as_float(r[h]) * p.scale_log2 : -INFINITY;
+          for (int c = 0; c < kASChains; c += 2) {
+            uint32_t r0[16], r1[16];
+            tmem_ld_32x32b_x16(ta + static_cast<uint32_t>(kAHeads * c), r0);
+            tmem_ld_32x32b_x16(ta + static_cast<uint32_t>(kAHeads * (c + 1)), r1);
+            tmem_wait_ld();
+#pragma unroll
+            for (int h = 0; h < kAHeads; ++h) {
+              const float sp = __uint_as_float(r0[h]) + __uint_as_float(r1[h]);
+              if (c == 0) half[h] = sp; else x[h] = ok ? (half[h] + sp) * p.scale_log2 : -INFINITY;
+            }
+          }
         } else {
           if (lane == 0) { *fail_a = 1; attn_fail(s, p.status); }
 #pragma unroll
           for (int h = 0; h < kAHeads; ++h) x[h] = -INFINITY;
         }
-#pragma unroll
-        for (int h = 0; h < kAHeads; ++h) {
-          float mx = x[h];
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-          if (lane == 0) s.tmax[warp - 4][h] = mx;
-        }
+        const float mx = warp_reduce16<true>(x, lane);
+        if ((lane & 1) == 0) s.tmax[warp - 4][reduce16_head(lane)] = mx;
       }
       named_bar_sync(1, 128);
       if (*fail_a) { finished = false; break; }
       // B: new running maximum, P, rescale of O^T
       float mnew[kAHeads], alpha[kAHeads];
-      bool grow = false;
+      bool grow = false;  // O^T holds earlier tiles that need rescaling
 #pragma unroll
       for (int h = 0; h < kAHeads; ++h) {
         const float mo = s.m[h];
-        const float mn = fmaxf(mo, fmaxf(s.tmax[0][h], s.tmax[1][h]));
+        const float mt = fmaxf(s.tmax[0][h], s.tmax[1][h]);
+        const float mn = (mo == -INFINITY || mt > mo + kRescaleLog2) ? fmaxf(mo, mt) : mo;
         mnew[h] = mn;
-        alpha[h] = mn == -INFINITY ? 1.f : exp2f(mo - mn);
-        grow |= mn > mo;
+        // before the first valid entry O and l are zero: nothing to rescale
+        alpha[h] = (mo == -INFINITY || mn == mo) ? 1.f : exp2f(mo - mn);
+        grow |= mo != -INFINITY && mn != mo;
       }
       if (sm) {
         // this P slot was last read by O^T += V^T P of tile i - 2
         const bool freed = i < 2 || __all_sync(0xffffffffu, mbar_wait(&s.done[k], ((i >> 1) & 1) ^ 1u, &s.abort, kWaitTimeoutNs));
         if (!freed && lane == 0) { *fail_b = 1; attn_fail(s, p.status); }
         uint8_t* pk = s.p[k];
+        float pr[kAHeads];
 #pragma unroll
         for (int h = 0; h < kAHeads; ++h) {
-          const float pv = x[h] == -INFINITY ? 0.f : exp2f(x[h] - mnew[h]);
+          const float pv = x[h] == -INFINITY ? 0.f : ex2_approx(x[h] - mnew[h]);
           const __nv_bfloat16 pb = __float2bfloat16_rn(pv);
           if (freed)
             *reinterpret_cast<__nv_bfloat16*>(pk + swz(h, row >> 3) + (row & 7) * 2) = pb;
-          float sum = __bfloat162float(pb);  // the sum of the probabilities the MMA uses
-#pragma unroll
-          for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-          if (lane == 0) s.tsum[warp - 4][h] = sum;
+          pr[h] = pv;  // l in fp32 (as the reference's softmax); only the MMA operand is bf16
         }
+        const float sum = warp_reduce16<false>(pr, lane);
+        if ((lane & 1) == 0) s.tsum[warp - 4][reduce16_head(lane)] = sum;
         fence_proxy_async_smem();
       }
       if (i > 0 && grow) {
@@ -328,13 +423,17 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
       tc_fence_before();
       named_bar_sync(1, 128);
       if (*fail_b) { finished = false; break; }
-      if (ep == 0) {
+      if (warp == 4) {  // one head per lane, then hand the tile to the MMA issuer
+        if (lane < kAHeads) {
+          float al = 1.f, mn = 0.f;
 #pragma unroll
-        for (int h = 0; h < kAHeads; ++h) {
-          s.l[h] = s.l[h] * alpha[h] + s.tsum[0][h] + s.tsum[1][h];
-          s.m[h] = mnew[h];
+          for (int h = 0; h < kAHeads; ++h)
+            if (h == lane) { al = alpha[h]; mn = mnew[h]; }
+          s.l[lane] = s.l[lane] * al + s.tsum[0][lane] + s.tsum[1][lane];
+          s.m[lane] = mn;
         }
-        mbar_arrive(&s.pfull[k]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.pfull[k]);
       }
     }
     if (finished && tiles > 0) {

@@ -485,11 +485,12 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
   }
 }
 
-// Merges the splits of each token: out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+// Merges the splits of each (token, head), one CTA each:
+// out = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
 __global__ void __launch_bounds__(kACkv) attn_combine_kernel(const float* part_o, const float* part_ml, int splits,
                                                              __nv_bfloat16* out, float* lse) {
-  const int t = blockIdx.x, d = threadIdx.x;
-  for (int h = 0; h < kAHeads; ++h) {
+  const int h = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+  {
     float mx = -INFINITY;
     for (int sp = 0; sp < splits; ++sp)
       mx = fmaxf(mx, part_ml[((static_cast<size_t>(t) * splits + sp) * kAHeads + h) * 2]);
@@ -502,7 +503,7 @@ __global__ void __launch_bounds__(kACkv) attn_combine_kernel(const float* part_o
       den += w * ls;
     }
     out[(static_cast<size_t>(t) * kAHeads + h) * kACkv + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
-    if (d == h) lse[static_cast<size_t>(t) * kAHeads + h] = den > 0.f ? mx + log2f(den) : -INFINITY;
+    if (d == 0) lse[static_cast<size_t>(t) * kAHeads + h] = den > 0.f ? mx + log2f(den) : -INFINITY;
   }
 }
 
@@ -564,7 +565,7 @@ cudaError_t launch_attn(const AttnLaunch& a, cudaStream_t stream) {
   attn_kernel<<<dim3(sp, a.num_tokens), kAThreads, kAttnSmemBytes, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || sp == 1) return e;
-  attn_combine_kernel<<<a.num_tokens, kACkv, 0, stream>>>(p.part_o, p.part_ml, sp, p.out, p.lse);
+  attn_combine_kernel<<<dim3(kAHeads, a.num_tokens), kACkv, 0, stream>>>(p.part_o, p.part_ml, sp, p.out, p.lse);
   return cudaGetLastError();
 }
 

@@ -13,11 +13,14 @@ order, :855-859 ordered keys, :897-905 / :1079-1097 short rows,
   * ``logits_numpy`` below: a vectorised numpy restatement of the scoring,
     used to cross-check the C code.
 
-Parity pinning: the reference ships no test vectors, and its own definition
+Parity pinning: the reference ships no test vectors, its own definition
 reference (a Python implementation in the contest dataset) is not available
-here.  The oracle is pinned against outputs of the reference's own CUDA
-kernel where those fixtures exist (``tests/golden/``); otherwise parity is
-unpinned beyond the known-answer tests in tests/test_oracle.py.
+here, and its CUDA kernel cannot run here.  The scoring stage is pinned to
+golden logits of DeepGEMM's published reference for paged FP8 MQA logits
+(as shipped in vLLM 0.22; tests/golden/indexer_logits_golden.npz, agreement
+to fp32 rounding, tests/test_oracle_pinned.py).  The selection stage (exact
+top-K, ties, -1 padding, physical ids) is restated from the reference
+kernel and checked by known answers (tests/test_oracle.py).
 """
 from __future__ import annotations
 

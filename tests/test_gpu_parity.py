@@ -62,6 +62,28 @@ def test_config0_full(oracle_mod):
     assert set(o[1].tolist()) == set(ids[1].tolist())
 
 
+def test_logits_match_published_reference_golden(oracle_mod):
+    """GPU logits (every row scored) against the golden logits of DeepGEMM's
+    published paged FP8 MQA logits reference (tests/golden/)."""
+    import sys
+    from pathlib import Path
+    gdir = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(gdir))
+    import make_indexer_logits_golden as G
+    z = np.load(gdir / "indexer_logits_golden.npz")
+    inp = G.inputs()
+    assert G.digest(inp) == str(z["sha256"])
+    ids, glog, status = gpu_run(inp)
+    assert status == 0
+    d = inp.numpy()
+    _, mag = oracle_mod.logits(d["q"], d["k_cache"], d["weights"], d["seq_lens"], d["block_table"],
+                               num_pages=d["num_pages"], nthreads=8, with_mag=True)
+    g = np.concatenate([glog[b, :L] for b, L in enumerate(G.LENS)])
+    m = np.concatenate([mag[b, :L] for b, L in enumerate(G.LENS)])
+    assert np.all(np.abs(g - z["logits"]) <= 1e-4 * (np.abs(z["logits"]) + m))
+    check(oracle_mod, inp, ids, glog)
+
+
 def test_config1_rows(oracle_mod):
     inp = W.config_inputs(1, rows=6)
     ids, glog, status = gpu_run(inp)

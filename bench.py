@@ -401,9 +401,11 @@ def bench_ours(args, world, rank, local):
 def bench_split(args, world, rank, local):
     """Config 3: one 131072-token row split by page range over the ranks
     (strong scaling).  A step = local scoring + local top-2048 pairs
-    (dsai_run_pairs), NCCL all-gather of the 2048 pairs of every rank, merge
-    (dsai_merge_pairs).  Every rank builds the same seeded row; a rank reads
-    only the pages of its range."""
+    (dsai_run_pairs), one NCCL all-gather of the 2048 (score, token) pairs of
+    every rank (packed in one buffer), merge (dsai_merge_pairs).  Every rank
+    builds the same seeded row; a rank reads only the pages of its range.
+    The row's pool (9.5 MB) fits in L2, so steps rotate over 16 copies of it
+    (152 MB, larger than L2)."""
     import torch.distributed as dist
     from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import distributed as D
     from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import merge_pairs, run_pairs
@@ -416,20 +418,20 @@ def bench_split(args, world, rank, local):
     local_len = max(0, min(L, p1 * 64) - p0 * 64)
     bt_local = g.block_table[:, p0:p1].contiguous()
     sl_local = torch.tensor([local_len], dtype=torch.int32, device=dev)
-    sc = torch.empty((1, 2048), dtype=torch.float32, device=dev)
-    tk = torch.empty((1, 2048), dtype=torch.int32, device=dev)
-    all_sc = torch.empty(world * 2048, dtype=torch.float32, device=dev)
-    all_tk = torch.empty(world * 2048, dtype=torch.int32, device=dev)
+    pairs = torch.empty((2, 2048), dtype=torch.int32, device=dev)   # scores (fp32 bits), tokens
+    sc, tk = pairs[0].view(torch.float32).view(1, 2048), pairs[1].view(1, 2048)
+    all_pairs = torch.empty((world, 2, 2048), dtype=torch.int32, device=dev)
+    pools = [g.k_cache] + [g.k_cache.clone() for _ in range(15)]  # 16 x 9.5 MB > L2
     bt_full = g.block_table[0].contiguous()
     sl_full = g.seq_lens[:1].contiguous()
     out = torch.empty(2048, dtype=torch.int32, device=dev)
 
-    def step():
-        run_pairs(g.q, g.k_cache, g.weights, sl_local, bt_local, p0 * 64, sc, tk)
+    def step(i=0):
+        run_pairs(g.q, pools[i % len(pools)], g.weights, sl_local, bt_local, p0 * 64, sc, tk)
         if world > 1:
-            dist.all_gather_into_tensor(all_sc, sc.view(-1))
-            dist.all_gather_into_tensor(all_tk, tk.view(-1))
-            merge_pairs(all_sc, all_tk, bt_full, sl_full, out)
+            dist.all_gather_into_tensor(all_pairs.view(-1), pairs.view(-1))
+            merge_pairs(all_pairs[:, 0].reshape(-1).view(torch.float32), all_pairs[:, 1].reshape(-1),
+                        bt_full, sl_full, out)
         else:
             merge_pairs(sc.view(-1), tk.view(-1), bt_full, sl_full, out)
 
@@ -452,8 +454,8 @@ def bench_split(args, world, rank, local):
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        step()
+    for i in range(args.steps):
+        step(i)
     e1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
@@ -470,6 +472,7 @@ def bench_split(args, world, rank, local):
         "us_per_call": round(ms * 1e3, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> f32 (scores), u32 keys (select)", "data": "synthetic (seeded, generated on device)",
         "config": {"workload": f"config3: {W.CONFIGS[3]}", "seq_len": L, "pages_per_rank": p1 - p0, "seed": seed,
+                   "l2": "16 rotating copies of the 9.5 MB page pool (152 MB > 126 MB L2)",
                    "parallelism": f"page-range split, NCCL all-gather of 2048 (score, token) pairs per rank x{world}"},
         "gpu_launches": args.steps * 3,
         "clocks": clk,

@@ -342,6 +342,47 @@ def bench_ours(args, world, rank, local):
     e2e_ms = float(te.item()) / e2e_steps
     e2e_value = alg * world / (e2e_ms / 1e3) / 1e9
 
+    # ---- a decode step with the index-K cache resident on the device: per
+    # step the new token of every row (bf16 keys, slot ids), q, weights,
+    # seq_lens and the block table cross PCIe, the writer stores the new keys
+    # into their pages, the indexer runs, the ids come back
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import write_index_k
+    kc_dev = base.k_cache.clone()
+    new_k = torch.randn((base.rows, 128), dtype=torch.bfloat16).pin_memory()
+    sl_h = base.seq_lens.cpu()
+    last = (sl_h - 1).clamp_min(0).long()
+    slot_h = (base.block_table.cpu()[torch.arange(base.rows), last // 64].long() * 64 + last % 64).to(torch.int32)
+    host_d = {"q": host["q"], "weights": host["weights"], "seq_lens": host["seq_lens"],
+              "block_table": host["block_table"], "new_k": new_k, "slots": slot_h.pin_memory()}
+    dev_d = {k: torch.empty_like(v, device=dev) for k, v in host_d.items()}
+    h2d_step = sum(v.numel() * v.element_size() for v in host_d.values())
+
+    def decode_step():
+        for k, v in host_d.items():
+            dev_d[k].copy_(v, non_blocking=True)
+        write_index_k(dev_d["new_k"], dev_d["slots"], kc_dev)
+        if R == 1:
+            kernel(dev_d["q"], kc_dev, dev_d["weights"], dev_d["seq_lens"], dev_d["block_table"], out_d)
+        else:
+            run(dev_d["q"], kc_dev, dev_d["weights"], dev_d["seq_lens"], dev_d["block_table"], out_d,
+                rows_per_seq=R)
+        out_h.copy_(out_d, non_blocking=True)
+
+    for _ in range(3):
+        decode_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0.record()
+    for _ in range(e2e_steps):
+        decode_step()
+    f1.record()
+    torch.cuda.synchronize()
+    td = torch.tensor([f0.elapsed_time(f1)], device=dev)
+    if world > 1:
+        dist.all_reduce(td, op=dist.ReduceOp.MAX)
+    dec_ms = float(td.item()) / e2e_steps
+
     if rank != 0:
         return None
     peak, peak_src = measured_hbm_peak()
@@ -387,6 +428,10 @@ def bench_ours(args, world, rank, local):
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "path": ("kernel(...) drop-in" if R == 1 else f"run(..., rows_per_seq={R})") + ", pinned host inputs"},
+        "e2e_decode_step": {"value": round(alg * world / (dec_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                            "us_per_step": round(dec_ms * 1e3, 2), "h2d_bytes_per_step": h2d_step, "d2h_bytes_per_step": d2h,
+                            "path": "index-K cache resident on the device; per step the new token of every row "
+                                    "(write_index_k), q, weights, seq_lens, block_table H2D, then the indexer, ids D2H"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk,
     }

@@ -103,6 +103,49 @@ def test_args_struct_layout_matches_header(tmp_path):
     assert got == want
 
 
+def test_sparse_attn_checked_without_device(dsai_lib):
+    """The sparse attention validates its arguments before it touches the
+    device; its workspace is a 256-B header at least."""
+    assert dsai_lib.dsai_sparse_attn(None, None, 0, None) == _lib.E_INVALID
+    a = _lib.DsaiAttnArgs(num_tokens=0, num_pages=4)
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), None, 0, None) == 0  # nothing to do
+    a = _lib.DsaiAttnArgs(num_tokens=-1, num_pages=4)
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), None, 0, None) == _lib.E_INVALID
+    a = _lib.DsaiAttnArgs(num_tokens=70000, num_pages=4)
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), None, 0, None) == _lib.E_INVALID
+    assert b"65535" in dsai_lib.dsai_last_error()
+    a = _lib.DsaiAttnArgs(q_nope=16, q_pe=32, ckv_cache=48, kpe_cache=None, sparse_indices=64, output=80, lse=96,
+                          sm_scale=0.1, num_tokens=2, num_pages=4)
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), 256, 1 << 20, None) == _lib.E_INVALID
+    assert b"NULL" in dsai_lib.dsai_last_error()
+    a.kpe_cache, a.q_pe = 64, 40  # q_pe not 16-B aligned
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), 256, 1 << 20, None) == _lib.E_INVALID
+    a.q_pe, a.sm_scale = 32, float("inf")
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), 256, 1 << 20, None) == _lib.E_INVALID
+    a.sm_scale = 0.1
+    assert dsai_lib.dsai_sparse_attn(ctypes.byref(a), 300, 1 << 20, None) == _lib.E_WORKSPACE
+    assert dsai_lib.dsai_sparse_attn_workspace_size(-1) == 0
+    assert dsai_lib.dsai_sparse_attn_workspace_size(0) >= 256
+
+
+def test_attn_args_struct_layout_matches_header(tmp_path):
+    import shutil
+    import subprocess
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f[0] for f in _lib.DsaiAttnArgs._fields_]
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "dsai.h"', "int main(void) {"]
+    lines += [f'  printf("%zu\\n", offsetof(dsai_attn_args, {f}));' for f in fields]
+    lines += ['  printf("%zu\\n", sizeof(dsai_attn_args));', "  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert got == [getattr(_lib.DsaiAttnArgs, f).offset for f in fields] + [ctypes.sizeof(_lib.DsaiAttnArgs)]
+
+
 def test_merge_and_status_reject_null(dsai_lib):
     assert dsai_lib.dsai_merge_pairs(None, None, -1, None, 4, None, None, None) == -1
     assert dsai_lib.dsai_merge_pairs(None, None, 4, 16, 4, 16, 16, None) == -1

@@ -604,13 +604,13 @@ struct WideSmem {
   int small_count;
   int eq_count;
   int extreme[3];  // first-digit bins 0 and 4088..4095 (NaN, infinities) are not empty
-  uint64_t vbar[kCPer / 4];  // one bulk copy of 4 * kWThreads logits per barrier
 };
 
 constexpr int kWideSmemBytes = static_cast<int>(sizeof(WideSmem));
 static_assert(kWideSmemBytes <= 232448, "the wide CTA must fit");
 static_assert(kBins2 == kWThreads && kHistBins == 4 * kWThreads, "bin ownership");
 static_assert(kSmall * 16 == kWThreads, "the final ranking uses 16 threads per key");
+static_assert(kCPer / 4 == 8, "eight cp.async groups per round");
 
 // One 1024-thread CTA per row: no cross-CTA traffic, and no block-wide scan
 // in the pass (output and candidate slots come from one shared atomic per
@@ -653,9 +653,6 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     return;
   }
   if (tid == 0) {
-#pragma unroll
-    for (int u = 0; u < kCPer / 4; ++u) sm100::mbar_init(&s.vbar[u], 1);
-    sm100::fence_mbar_init();
     s.out_count = 0;
     s.cand_count = 0;
     s.small_count = 0;
@@ -675,24 +672,23 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
   const uint4 hx = g4[tid];
 
-  // A round of logits into shared memory by thread 0: one bulk copy per
-  // group of 4 * kWThreads entries, each on its own barrier, so that the
-  // classification of a group starts as soon as it has landed.  Linear
-  // copies land in the [group][thread] float4 layout the threads read.  The
-  // row buffer is padded to 64 entries, so the copied size rounds up to 16 B
-  // inside it.
-  const uint64_t pol = sm100::l2_policy_evict_first();
+  // A round of logits into shared memory: every thread copies its own 16 B
+  // of each group of 4 * kWThreads entries (one cp.async group per group of
+  // entries) and reads only those slots, so it waits for its own copies
+  // (cp.async.wait_group) and the classification of a group starts as soon
+  // as it has landed.  The row buffer is padded to 64 entries, so a float4
+  // that starts below the row's end stays inside it; past the end the copy
+  // zero-fills without reading.
   auto load_round = [&](int base) {
     const int n = min(L - base, kWRound);
-#pragma unroll 1
-    for (int u = 0; u * 4 * kWThreads < n; ++u) {
-      const int e0 = u * 4 * kWThreads;
-      const uint32_t bytes = static_cast<uint32_t>(((min(n - e0, 4 * kWThreads) + 3) / 4) * 16);
-      sm100::mbar_arrive_expect_tx(&s.vbar[u], bytes);
-      sm100::bulk_load(&s.vals[u][0], row + base + e0, bytes, &s.vbar[u], pol);
+#pragma unroll
+    for (int u = 0; u < kCPer / 4; ++u) {
+      const int e = u * 4 * kWThreads + 4 * tid;
+      sm100::cp_async_16(&s.vals[u][tid], e < n ? row + base + e : row, e < n ? 16u : 0u);
+      sm100::cp_async_commit_group();
     }
   };
-  if (tid == 0) load_round(0);
+  load_round(0);
 
   uint32_t h1[4] = {hx.x, hx.y, hx.z, hx.w};
   if (tid == 0) s.extreme[0] = h1[0] != 0u;
@@ -723,13 +719,8 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     }
   };
 
-  bool copies_ok = true;
-  int round = 0;
-  for (int base = 0; base < L; base += kWRound, ++round) {
-    if (base != 0) {
-      __syncthreads();  // every thread is done with the previous round
-      if (tid == 0) load_round(base);
-    }
+  for (int base = 0; base < L; base += kWRound) {
+    if (base != 0) load_round(base);  // each thread refills only its own slots
     uint32_t gtm = 0u, inm = 0u;
     // Groups u < groups hold entries below L; only the last one can be
     // partial (entries of group u end at base + 4 * (u + 1) * kWThreads).
@@ -737,8 +728,15 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
 #pragma unroll
     for (int u = 0; u < kCPer / 4; ++u) {
       if (u < groups) {
-        if (!sm100::mbar_wait(&s.vbar[u], static_cast<uint32_t>(round & 1), nullptr, kWaitTimeoutNs)) {
-          copies_ok = false;  // classified from whatever landed; reported below
+        switch (u) {  // this thread's copies of groups 0..u have landed
+          case 0: sm100::cp_async_wait_group<7>(); break;
+          case 1: sm100::cp_async_wait_group<6>(); break;
+          case 2: sm100::cp_async_wait_group<5>(); break;
+          case 3: sm100::cp_async_wait_group<4>(); break;
+          case 4: sm100::cp_async_wait_group<3>(); break;
+          case 5: sm100::cp_async_wait_group<2>(); break;
+          case 6: sm100::cp_async_wait_group<1>(); break;
+          default: sm100::cp_async_wait_group<0>(); break;
         }
         const float4 w = s.vals[u][tid];
         if (fast_skip && fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) < f_lo) continue;
@@ -782,17 +780,8 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
       atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
     }
   }
+  sm100::cp_async_wait_group<0>();  // groups past the row's end (zero-fills) too
   __syncthreads();  // candidates, second-digit counts and output slots are final
-  if (!copies_ok) {
-    report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
-    // Never leave with a bulk copy in flight into this CTA's shared memory.
-    if (tid == 0) {
-      const int last = (L - 1) / kWRound;
-      const int n = min(L - last * kWRound, kWRound);
-      for (int u = 0; u * 4 * kWThreads < n; ++u)
-        sm100::mbar_wait(&s.vbar[u], static_cast<uint32_t>(last & 1), nullptr, kWaitTimeoutNs);
-    }
-  }
 
   if (!listed) {
     // More keys in the pivot bin than the list holds: the second digit over

@@ -16,7 +16,7 @@
 //   warps 0-3  gather: each tile's 64 ckv rows (1 KB) and kpe rows (128 B)
 //              with 16-B cp.async into a 128-B-swizzled [9 k-blocks][64 rows]
 //              buffer (two buffers); -1 and out-of-range slots zero-fill.
-//   warp 8     MMA issuer: S^T = K Q^T (tcgen05 kind::f16 M128 N16 K16, bf16
+//   warps 8-9  MMA issuers (one thread each): S^T = K Q^T (tcgen05 kind::f16 M128 N16 K16, bf16
 //              -> f32 in TMEM; rows 64-127 of the M = 128 operand are not
 //              used) as four independent accumulator chains over the 36
 //              K-steps (a single chain waits ~100 cycles per MMA on its
@@ -55,7 +55,7 @@ constexpr int kABufBytes = kAKBlocks * kABlockBytes;     // 72 KB
 constexpr int kAQBlockBytes = kAHeads * 128;             // 2 KB
 constexpr int kAQBytes = kAKBlocks * kAQBlockBytes;      // 18 KB
 constexpr int kAPBytes = kAHeads * kATile * 2;           // 2 KB
-constexpr int kAThreads = 288;
+constexpr int kAThreads = 320;  // warps 0-3 gather, 4-7 softmax/epilogue, 8 score MMAs, 9 V^T P MMAs
 constexpr int kASChains = 4;     // partial score accumulators per tile
 constexpr int kATmemCols = 256;  // S: 2 slots x 4 chains x 16 columns, O^T: 4 x 16 columns from column 128
 constexpr int kAOCol = 2 * kASChains * kAHeads;
@@ -93,7 +93,7 @@ struct AttnSmem {
   uint64_t sfull[2];            // S^T of the tile in this slot in TMEM
   uint64_t pfull[2];            // P of the tile in this slot written (and O rescaled)
   uint64_t qfull;
-  uint64_t drain;
+  uint64_t drain[2];            // per MMA-issuing thread
   uint32_t tmem_base;
   int abort;
   int fail_a;                   // epilogue failures before / after the tile's first named barrier
@@ -190,7 +190,8 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
       mbar_init(&s.pfull[i], 1);
     }
     mbar_init(&s.qfull, 128);
-    mbar_init(&s.drain, 1);
+    mbar_init(&s.drain[0], 1);
+    mbar_init(&s.drain[1], 1);
     for (int h = 0; h < kAHeads; ++h) {
       s.m[h] = -INFINITY;
       s.l[h] = 0.f;
@@ -256,14 +257,16 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
       mbar_arrive(&s.full[b]);
     }
   } else if (warp == 8) {
-    // ------------------------------------------------------------ MMA issuer
+    // ------------------------------------------------------------ score MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, kAHeads, false);
-      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, kAHeads, true);
       bool ok = mbar_wait(&s.qfull, 0, &s.abort, kWaitTimeoutNs);
-      auto issue_s = [&](int i) -> bool {
+      // The TMEM slot of tile i's scores was last read by the softmax of
+      // tile i - 2, which finished before that tile's V^T P, which freed the
+      // buffer this tile's rows came into.
+      for (int i = 0; i < tiles && ok; ++i) {
         const int b = i & 1;
-        if (!mbar_wait(&s.full[b], (i >> 1) & 1, &s.abort, kWaitTimeoutNs)) return false;
+        if (!mbar_wait(&s.full[b], (i >> 1) & 1, &s.abort, kWaitTimeoutNs)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d = tbase + static_cast<uint32_t>(kASChains * kAHeads * (i & 1));
         const uint64_t a0 = make_sw128_kmajor_desc(smem_u32(s.buf[b]));
@@ -278,26 +281,22 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
           umma_bf16(d + static_cast<uint32_t>(kAHeads * (n % kASChains)), a, q, idesc_s, n >= kASChains ? 1u : 0u);
         }
         umma_commit(&s.sfull[i & 1]);
-        return true;
-      };
-      if (ok && tiles > 0) ok = issue_s(0);
-      int next_s = 1;  // the next tile whose scores are not issued yet
-      for (int i = 0; i < tiles && ok; ++i) {
-        // While this tile's probabilities are computed, issue the next
-        // tile's scores if its rows have landed (never wait for them here:
-        // this tile's V^T P frees the buffer the gather needs next).
-        const uint64_t t0 = global_timer_ns();
-        while (!mbar_try_wait(&s.pfull[i & 1], (i >> 1) & 1)) {
-          if (next_s == i + 1 && next_s < tiles && mbar_try_wait(&s.full[next_s & 1], (next_s >> 1) & 1)) {
-            if (!issue_s(next_s)) { ok = false; break; }
-            ++next_s;
-          }
-          if (*reinterpret_cast<volatile int*>(&s.abort) || global_timer_ns() - t0 > kWaitTimeoutNs) {
-            ok = false;
-            break;
-          }
-        }
-        if (!ok) break;
+      }
+      if (!ok) attn_fail(s, p.status);
+      // Every MMA issued by this thread has completed once this arrives.
+      umma_commit(&s.drain[0]);
+      if (!mbar_wait(&s.drain[0], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ V^T P MMA issuer
+    // A thread of its own, so that a tile's V^T P (which frees the tile's
+    // buffer) never waits behind the next tile's 36 score MMAs.
+    if (lane == 0) {
+      constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, kAHeads, true);
+      bool ok = true;
+      for (int i = 0; i < tiles; ++i) {
+        if (!mbar_wait(&s.pfull[i & 1], (i >> 1) & 1, &s.abort, kWaitTimeoutNs)) { ok = false; break; }
         tc_fence_after();
         const int b = i & 1;
         const uint64_t v0 = make_sw128_mnmajor_desc(smem_u32(s.buf[b]), kABlockBytes);
@@ -312,14 +311,10 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
           }
         }
         umma_commit(&s.done[b]);
-        if (next_s == i + 1 && next_s < tiles) {
-          if (!issue_s(next_s)) { ok = false; break; }
-          ++next_s;
-        }
       }
       if (!ok) attn_fail(s, p.status);
-      umma_commit(&s.drain);
-      if (!mbar_wait(&s.drain, 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      umma_commit(&s.drain[1]);
+      if (!mbar_wait(&s.drain[1], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
     }
     __syncwarp();
   } else {

@@ -16,7 +16,7 @@
 //   warps 0-3  gather: each tile's 64 ckv rows (1 KB) and kpe rows (128 B)
 //              with 16-B cp.async into a 128-B-swizzled [9 k-blocks][64 rows]
 //              buffer (two buffers); -1 and out-of-range slots zero-fill.
-//   warps 8-9  MMA issuers (one thread each): S^T = K Q^T (tcgen05 kind::f16 M128 N16 K16, bf16
+//   warps 8-13 MMA issuers (one thread each; 4 for the scores, 2 for V^T P): S^T = K Q^T (tcgen05 kind::f16 M128 N16 K16, bf16
 //              -> f32 in TMEM; rows 64-127 of the M = 128 operand are not
 //              used) as four independent accumulator chains over the 36
 //              K-steps (a single chain waits ~100 cycles per MMA on its
@@ -55,7 +55,10 @@ constexpr int kABufBytes = kAKBlocks * kABlockBytes;     // 72 KB
 constexpr int kAQBlockBytes = kAHeads * 128;             // 2 KB
 constexpr int kAQBytes = kAKBlocks * kAQBlockBytes;      // 18 KB
 constexpr int kAPBytes = kAHeads * kATile * 2;           // 2 KB
-constexpr int kAThreads = 320;  // warps 0-3 gather, 4-7 softmax/epilogue, 8 score MMAs, 9 V^T P MMAs
+constexpr int kASIssuers = 4;   // threads issuing the score MMAs (one accumulator chain each)
+constexpr int kAOIssuers = 2;   // threads issuing the V^T P MMAs (two 128-dim blocks each)
+constexpr int kAWarpS = 8;      // first score-issuer warp; the V^T P issuers follow
+constexpr int kAThreads = 32 * (kAWarpS + kASIssuers + kAOIssuers);  // warps 0-3 gather, 4-7 softmax/epilogue
 constexpr int kASChains = 4;     // partial score accumulators per tile
 constexpr int kATmemCols = 256;  // S: 2 slots x 4 chains x 16 columns, O^T: 4 x 16 columns from column 128
 constexpr int kAOCol = 2 * kASChains * kAHeads;
@@ -93,12 +96,15 @@ struct AttnSmem {
   uint64_t sfull[2];            // S^T of the tile in this slot in TMEM
   uint64_t pfull[2];            // P of the tile in this slot written (and O rescaled)
   uint64_t qfull;
-  uint64_t drain[2];            // per MMA-issuing thread
+  uint64_t drain[kASIssuers + kAOIssuers];  // per MMA-issuing thread
   uint32_t tmem_base;
   int abort;
   int fail_a;                   // epilogue failures before / after the tile's first named barrier
   int fail_b;
 };
+
+static_assert(kASIssuers == kASChains, "one score issuer per accumulator chain");
+static_assert(4 % kAOIssuers == 0, "the V^T P issuers split the four 128-dim blocks");
 
 constexpr int kAttnSmemBytes = static_cast<int>(sizeof(AttnSmem)) + 1024;
 static_assert(kAttnSmemBytes <= 232448, "the attention CTA must fit");
@@ -185,13 +191,12 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.full[i], 128);
-      mbar_init(&s.done[i], 1);
-      mbar_init(&s.sfull[i], 1);
+      mbar_init(&s.done[i], kAOIssuers);  // every V^T P issuer commits
+      mbar_init(&s.sfull[i], kASIssuers);  // every score issuer commits
       mbar_init(&s.pfull[i], 1);
     }
     mbar_init(&s.qfull, 128);
-    mbar_init(&s.drain[0], 1);
-    mbar_init(&s.drain[1], 1);
+    for (int i = 0; i < kASIssuers + kAOIssuers; ++i) mbar_init(&s.drain[i], 1);
     for (int h = 0; h < kAHeads; ++h) {
       s.m[h] = -INFINITY;
       s.l[h] = 0.f;
@@ -256,8 +261,11 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
       fence_proxy_async_smem();
       mbar_arrive(&s.full[b]);
     }
-  } else if (warp == 8) {
-    // ------------------------------------------------------------ score MMA issuer
+  } else if (warp >= kAWarpS && warp < kAWarpS + kASIssuers) {
+    // ------------------------------------------------------------ score MMA issuers
+    // One thread per accumulator chain: the issue of a tcgen05.mma with
+    // N = 16 costs its thread ~40 ns, so the 36 K-steps are spread.
+    const int chain = warp - kAWarpS;
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_bf16_f32(128, kAHeads, false);
       bool ok = mbar_wait(&s.qfull, 0, &s.abort, kWaitTimeoutNs);
@@ -273,9 +281,9 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
         const uint64_t q0 = make_sw128_kmajor_desc(smem_u32(s.q));
         // K-step n (16 dims) goes to chain n % 4; descriptor start addresses
         // advance in 16-B units
-#pragma unroll 4
-        for (int n = 0; n < kAKBlocks * 4; ++n) {
-          const int kb = n >> 2, k16 = n & 3;
+#pragma unroll 3
+        for (int kb = 0; kb < kAKBlocks; ++kb) {  // this chain's K-steps n = 4 kb + chain
+          const int n = kASChains * kb + chain, k16 = chain;
           const uint64_t a = a0 + static_cast<uint64_t>((kb * kABlockBytes + k16 * 32) >> 4);
           const uint64_t q = q0 + static_cast<uint64_t>((kb * kAQBlockBytes + k16 * 32) >> 4);
           umma_bf16(d + static_cast<uint32_t>(kAHeads * (n % kASChains)), a, q, idesc_s, n >= kASChains ? 1u : 0u);
@@ -284,14 +292,15 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
       }
       if (!ok) attn_fail(s, p.status);
       // Every MMA issued by this thread has completed once this arrives.
-      umma_commit(&s.drain[0]);
-      if (!mbar_wait(&s.drain[0], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      umma_commit(&s.drain[chain]);
+      if (!mbar_wait(&s.drain[chain], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ V^T P MMA issuer
-    // A thread of its own, so that a tile's V^T P (which frees the tile's
-    // buffer) never waits behind the next tile's 36 score MMAs.
+  } else if (warp >= kAWarpS + kASIssuers) {
+    // ------------------------------------------------------------ V^T P MMA issuers
+    // Threads of their own, so that a tile's V^T P (which frees the tile's
+    // buffer) never waits behind the next tile's score MMAs.
+    const int oi = warp - kAWarpS - kASIssuers;
     if (lane == 0) {
       constexpr uint32_t idesc_o = make_idesc_bf16_f32(128, kAHeads, true);
       bool ok = true;
@@ -302,9 +311,9 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
         const uint64_t v0 = make_sw128_mnmajor_desc(smem_u32(s.buf[b]), kABlockBytes);
         const uint64_t p0 = make_sw128_kmajor_desc(smem_u32(s.p[b]));
 #pragma unroll
-        for (int j = 0; j < kATile / 16; ++j) {  // 16 entries per MMA; the 4 M blocks interleave
+        for (int j = 0; j < kATile / 16; ++j) {  // 16 entries per MMA; this thread's M blocks interleave
 #pragma unroll
-          for (int mb = 0; mb < 4; ++mb) {       // 128 ckv dims = 2 k-blocks per M block
+          for (int mb = oi * (4 / kAOIssuers); mb < (oi + 1) * (4 / kAOIssuers); ++mb) {  // 128 dims each
             const uint64_t a = v0 + static_cast<uint64_t>(((2 * mb) * kABlockBytes + j * 2048) >> 4);
             const uint64_t pd = p0 + static_cast<uint64_t>((j * 32) >> 4);
             umma_bf16(tbase + static_cast<uint32_t>(kAOCol + 16 * mb), a, pd, idesc_o, (i > 0 || j > 0) ? 1u : 0u);
@@ -313,8 +322,8 @@ __global__ void __launch_bounds__(kAThreads, 1) attn_kernel(const AttnParams p) 
         umma_commit(&s.done[b]);
       }
       if (!ok) attn_fail(s, p.status);
-      umma_commit(&s.drain[1]);
-      if (!mbar_wait(&s.drain[1], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      umma_commit(&s.drain[kASIssuers + oi]);
+      if (!mbar_wait(&s.drain[kASIssuers + oi], 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
     }
     __syncwarp();
   } else {

@@ -730,7 +730,10 @@ def bench_attn(args, world, rank, local):
                    "l2": f"pool {(ckv.numel() + kpe.numel()) * 2 / 1e6:.0f} MB (> 126 MB L2), 2 rotating index sets"},
         "roofline": {"kernel": "attn_kernel (+ attn_combine_kernel)", "bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(gbs / peak, 4),
-                     "algorithmic_bytes_per_launch": alg, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg,
+                     "traffic": 152_770_560 + 4_194_048 if T == 64 else None,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_kernel, one launch "
+                                        "(profiles/attn_kernel_t64.md)" if T == 64 else "no ncu capture for this size"),
                      "tensor": {"achieved": round(flops / (us / 1e6) / 1e12, 1), "unit": "TFLOP/s",
                                 "algorithmic_flops_per_launch": flops}},
         "gpu_launches": 2 * args.steps,

@@ -165,8 +165,8 @@ int prepare_hist(void* ws, int32_t rows, cudaStream_t stream) {
   }
   if (rows > clean) {
     uint8_t* base = static_cast<uint8_t*>(ws) + dsai::kWsHeader +
-                    static_cast<size_t>(clean) * dsai::kHistBins * sizeof(uint32_t);
-    const size_t bytes = static_cast<size_t>(rows - clean) * dsai::kHistBins * sizeof(uint32_t);
+                    static_cast<size_t>(clean) * dsai::kHistStride * sizeof(uint32_t);
+    const size_t bytes = static_cast<size_t>(rows - clean) * dsai::kHistStride * sizeof(uint32_t);
     cudaError_t e = cudaMemsetAsync(base, 0, bytes, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(histograms)");
   }
@@ -175,9 +175,16 @@ int prepare_hist(void* ws, int32_t rows, cudaStream_t stream) {
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// Workspace layout: [header 256 B | per-row first-digit histograms | logits].
+// Workspace layout: [header 256 B | per-row histogram blocks (4096 bins and
+// 4 counters; 256-B rounded) | per-row pivot-bin lists of the split selection
+// (kSplitCap keys, then kSplitCap values) | logits (256-B rounded)].
 size_t hist_bytes(int32_t rows) {
-  return static_cast<size_t>(rows) * dsai::kHistBins * sizeof(uint32_t);
+  const size_t b = static_cast<size_t>(rows) * dsai::kHistStride * sizeof(uint32_t);
+  return (b + 255) & ~static_cast<size_t>(255);
+}
+
+size_t cand_bytes(int32_t rows) {
+  return static_cast<size_t>(rows) * dsai::kSplitCap * 2 * sizeof(uint32_t);
 }
 
 size_t logits_bytes(int32_t rows, int32_t max_pages) {
@@ -189,8 +196,13 @@ uint32_t* ws_hist(void* ws) {
   return reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader);
 }
 
+uint32_t* ws_cand(void* ws, int32_t rows) {
+  return reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader + hist_bytes(rows));
+}
+
 float* ws_logits(void* ws, int32_t rows) {
-  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader + hist_bytes(rows));
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + dsai::kWsHeader + hist_bytes(rows) +
+                                  cand_bytes(rows));
 }
 
 int check_args(const dsai_args* a, void* ws, size_t ws_bytes, bool need_ids) {
@@ -245,7 +257,7 @@ int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, 
     p.seq_lens = a->seq_lens + r0;
     p.block_table = a->block_table + static_cast<size_t>(r0) * a->max_pages;
     p.logits = logits + static_cast<size_t>(r0) * ld;
-    p.hist = hist + static_cast<size_t>(r0) * dsai::kHistBins;
+    p.hist = hist + static_cast<size_t>(r0) * dsai::kHistStride;
     p.status = status;
     p.rows = n;
     p.max_pages = a->max_pages;
@@ -271,7 +283,7 @@ extern "C" {
 
 size_t dsai_workspace_size(int32_t rows, int32_t max_pages) {
   if (rows < 0 || max_pages < 0) return 0;
-  return dsai::kWsHeader + hist_bytes(rows) + logits_bytes(rows, max_pages);
+  return dsai::kWsHeader + hist_bytes(rows) + cand_bytes(rows) + logits_bytes(rows, max_pages);
 }
 
 int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -321,6 +333,7 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   sp.logits = logits;
   sp.ld = a->max_pages * dsai::kPage;
   sp.hist = hist;
+  sp.cand = ws_cand(workspace, a->rows);
   sp.seq_lens = a->seq_lens;
   sp.block_table = a->block_table;
   sp.rows = a->rows;
@@ -362,6 +375,7 @@ int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, 
   sp.logits = logits;
   sp.ld = a->max_pages * dsai::kPage;
   sp.hist = hist;
+  sp.cand = ws_cand(workspace, a->rows);
   sp.seq_lens = a->seq_lens;
   sp.block_table = a->block_table;
   sp.rows = a->rows;

@@ -33,6 +33,12 @@ constexpr int kMaxRowsPerLaunch = 1024;
 // clears it again for the next call.
 constexpr int kHistBits = 12;
 constexpr int kHistBins = 1 << kHistBits;
+// A row's histogram block in the workspace: the 4096 bins, then four u32 of
+// per-row counters used by the split selection (output and candidate slots
+// taken, chunks finished).  They are zero between calls like the bins.
+constexpr int kHistStride = kHistBins + 4;
+// Pivot-bin keys the split selection keeps per row (workspace lists).
+constexpr int kSplitCap = 8192;
 
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s bound on any on-chip wait
 

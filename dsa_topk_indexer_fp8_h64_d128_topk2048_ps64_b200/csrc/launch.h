@@ -12,7 +12,7 @@ struct ScoreLaunch {
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* logits;      // [rows, ld]
-  uint32_t* hist;     // [rows, kHistBins] first-digit histograms (zero on entry)
+  uint32_t* hist;     // [rows, kHistStride] first-digit histograms (zero on entry)
   int* status;
   int rows;
   int max_pages;
@@ -60,7 +60,8 @@ cudaError_t launch_attn(const AttnLaunch& a, cudaStream_t stream);
 struct SelectLaunch {
   const float* logits;  // [rows, ld]
   int ld;
-  uint32_t* hist;       // [rows, kHistBins] from the scoring launch; cleared here
+  uint32_t* hist;       // [rows, kHistStride] from the scoring launch; cleared here
+  uint32_t* cand;       // [rows, 2, kSplitCap] pivot-bin lists of the split selection
   const int32_t* seq_lens;
   const int32_t* block_table;
   int rows;

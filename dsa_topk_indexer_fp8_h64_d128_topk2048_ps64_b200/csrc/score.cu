@@ -56,7 +56,7 @@ struct ScoreParams {
   const int32_t* seq_lens;
   const int32_t* block_table;
   float* logits;
-  uint32_t* hist;     // [rows, kHistBins] (rows of this launch)
+  uint32_t* hist;     // [rows, kHistStride] (rows of this launch)
   int* status;
   int rows;
   int max_pages;
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           L = row_len(p.seq_lens, cur_row, p.max_pages, nullptr);
           hist_row = L > kTopK;  // only rows that go through the radix select
           out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
-          hist_g = p.hist + static_cast<size_t>(cur_row) * kHistBins;
+          hist_g = p.hist + static_cast<size_t>(cur_row) * kHistStride;
         }
         // Waits are decided warp-wide: the warp runs warp-collective steps below.
         if (!__all_sync(0xffffffffu, mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs))) {

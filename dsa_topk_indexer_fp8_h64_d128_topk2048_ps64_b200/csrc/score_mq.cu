@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(MqTraits<R>::kThreads, 1)
           // slots, aggregating equal bins in the warp first (the per-row
           // scorer's match) costs more than the L2 reductions it saves.
           const uint32_t bin = ordered_key(logit) >> (32 - kHistBits);
-          if (live) atomicAdd(p.hist + b * kHistBins + bin, 1u);  // RED
+          if (live) atomicAdd(p.hist + static_cast<size_t>(b) * kHistStride + bin, 1u);  // RED
         }
         if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
         if (++sslot == kMqScaleSlots) { sslot = 0; sphase ^= 1u; }

@@ -21,9 +21,15 @@
 //            else a third digit is counted) are ranked by one warp, which
 //            fills the last slots (ties at the pivot in list order).
 //
-// Few long rows (select_rows_kernel): one thread-block cluster of C CTAs
-// per row (C = 2..8, so that every CTA is resident at once), 256 threads per
-// CTA, three CTAs per SM.
+// Few rows (select_split_kernel, described above the kernel): several
+// 256-thread CTAs per row, 4096 tokens each, that share the row's output
+// slots through atomics on counters in the workspace; the CTA that finishes
+// the row last refines it.
+//
+// Few long rows, the earlier shape kept for comparison (select_rows_kernel,
+// used with DSAI_SELECT=rows): one thread-block cluster of C CTAs per row
+// (C = 2..8, so that every CTA is resident at once), 256 threads per CTA,
+// three CTAs per SM.
 //   digit 1  the leader CTA finds the pivot bin and hands it to the
 //            cluster's CTAs (distributed shared memory, one cluster barrier)
 //            while their first round of logits is copied into shared memory;
@@ -50,6 +56,8 @@
 // The merge of (score, token) lists from a page-range split runs the same
 // three digits in one 512-thread CTA over the list.
 #include <cfloat>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "launch.h"
@@ -345,7 +353,7 @@ __global__ void __launch_bounds__(NT, SelShape<NT>::kCtasPerSm) select_rows_kern
   if (bt_cached)
     for (int i = tid; i < npg; i += NT) s.bt[i] = bt_row[pg0 + i];
 
-  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistBins;
+  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistStride;
   if (leader) {
     // Digit 1 from the scoring kernel's histogram (cleared below once used):
     // coalesced loads, staged so that each thread owns consecutive bins; the
@@ -669,7 +677,7 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   grid_dep_launch_dependents();
   // Digit 1: thread t owns bins [4t, 4t + 4) of the scoring kernel's
   // histogram (one coalesced 16-B load), cleared for the next call once read.
-  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistBins);
+  uint4* g4 = reinterpret_cast<uint4*>(p.hist + static_cast<size_t>(b) * kHistStride);
   const uint4 hx = g4[tid];
 
   // A round of logits into shared memory: every thread copies its own 16 B
@@ -878,6 +886,374 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   }
 }
 
+// ------------------------------------------------------------ several CTAs per row
+
+// Split selection: CTA (b, c) of a grid of rows x chunks_per_row handles
+// tokens [4096c, 4096c + 4096) of row b; CTAs past the row's end leave at
+// once.  Every CTA of a row finds the same pivot bin from the row's
+// histogram, classifies its chunk, takes output and list slots with one
+// 64-bit atomic on the row's counters, emits the keys above the pivot bin
+// and appends the keys in it to the row's list in the workspace.  The CTA
+// that finishes last (a ticket counter) refines over that list: the second
+// digit, then the <= 64 keys sharing the 22-bit prefix ranked by the block
+// (or a third digit); it also clears the row's histogram and counters for
+// the next call.  No CTA waits for another: the last one only reads what the
+// others published before they took their tickets.  A long row is thus
+// streamed by many SMs at once instead of one (one SM pulls ~50 GB/s of
+// logits from L2).
+constexpr int kSThreads = 256;
+constexpr int kSPer = 16;                   // entries per thread
+constexpr int kSChunk = kSThreads * kSPer;  // 4096 tokens per CTA
+constexpr int kSSmall = 64;                 // second-digit bin small enough to rank directly
+constexpr int kSStage = kSChunk / 2;        // list entries the last CTA stages in shared memory
+
+// The row's counters, stored after its 4096 histogram bins (zero between
+// calls).
+struct RowCtl {
+  unsigned long long slots;  // output slots (low 32 bits) and list slots (high 32 bits) taken
+  unsigned int done;         // CTAs of the row finished
+  unsigned int pad;
+};
+static_assert(sizeof(RowCtl) == (kHistStride - kHistBins) * sizeof(uint32_t), "counter block");
+
+struct SplitSmem {
+  union {
+    float4 vals[kSPer / 4][kSThreads];  // the chunk's logits
+    struct {
+      uint32_t key[kSStage];            // last CTA: the first entries of the row's
+      int32_t val[kSStage];             // pivot-bin list (the rest stays in L2)
+    } list;
+  } u;
+  uint32_t hist[kBins2];                // second (then third) digit histogram
+  int32_t bt[kSChunk / kPage];          // the chunk's pages
+  uint32_t small_key[kSSmall];
+  int32_t small_val[kSSmall];
+  Scan sc;
+  int extreme[2];  // first-digit bins 0 and 4088..4095 (NaN, infinities) are not empty
+  int base_out;
+  int base_cand;
+  int last;
+  int out_count;
+  int n_cand;
+  int small_count;
+  int eq_count;
+};
+
+constexpr int kSplitSmemBytes = static_cast<int>(sizeof(SplitSmem));
+static_assert(sizeof(SplitSmem::u) == kSPer / 4 * kSThreads * 16, "the list staging reuses the logits buffer");
+static_assert(kSStage % kSThreads == 0, "list staging");
+static_assert(kSThreads == 4 * kSSmall, "four threads rank each of the 64 keys");
+
+template <bool kIds>
+__global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const SelectLaunch p, int chunks_per_row) {
+  constexpr int kHPer = kHistBins / kSThreads;  // 16 first-digit bins per thread
+  constexpr int kB2Per = kBins2 / kSThreads;    // 4 refinement bins per thread
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  SplitSmem& s = *reinterpret_cast<SplitSmem*>(smem_raw);
+  const int tid = threadIdx.x;
+  const int b = static_cast<int>(blockIdx.x) / chunks_per_row;
+  const int c = static_cast<int>(blockIdx.x) - b * chunks_per_row;
+  // Before the wait on the scoring kernel: seq_lens and the block table,
+  // which it does not write.
+  const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
+  const int nch = L > kTopK ? (L + kSChunk - 1) / kSChunk : 1;
+  if (c >= nch) return;  // CTA (b, 0) exists for every row, and it waits
+  const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
+  const float* row = p.logits + static_cast<size_t>(b) * p.ld;
+  RowOut<kIds> out;
+  out.ids = kIds ? p.out_ids + static_cast<size_t>(b) * kTopK : nullptr;
+  out.scores = kIds ? nullptr : p.out_scores + static_cast<size_t>(b) * kTopK;
+  out.tokens = kIds ? nullptr : p.out_tokens + static_cast<size_t>(b) * kTopK;
+  out.offset = p.token_offset;
+
+  if (L <= kTopK) {  // every token is selected
+    if constexpr (!kIds) grid_dep_wait();  // the pairs carry the scores
+    for (int i = tid; i < kTopK; i += kSThreads) {
+      if constexpr (kIds) {
+        out.ids[i] = i < L ? physical_id(bt_row, i) : -1;
+      } else {
+        out.scores[i] = i < L ? row[i] : -INFINITY;
+        out.tokens[i] = i < L ? i + p.token_offset : -1;
+      }
+    }
+    if constexpr (kIds) grid_dep_wait();  // the grid completes after the scoring grid
+    grid_dep_launch_dependents();
+    return;
+  }
+  const int t0 = c * kSChunk;
+  const int t1 = min(L, t0 + kSChunk);
+  const int pg0 = t0 / kPage;
+  if constexpr (kIds) {
+    const int npg = (t1 - t0 + kPage - 1) / kPage;
+    for (int i = tid; i < npg; i += kSThreads) s.bt[i] = bt_row[pg0 + i];
+  }
+  uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistStride;
+  RowCtl* ctl = reinterpret_cast<RowCtl*>(g_hist + kHistBins);
+  uint32_t* list_key = p.cand + static_cast<size_t>(b) * (2 * kSplitCap);
+  int32_t* list_val = reinterpret_cast<int32_t*>(list_key + kSplitCap);
+
+  // The scoring kernel's logits and histograms are complete past this wait.
+  grid_dep_wait();
+  grid_dep_launch_dependents();
+  // Digit 1: thread t owns bins [16t, 16t + 16) of the row's histogram.
+  // These loads go out before the logits' copies, which would otherwise
+  // queue ahead of them.
+  uint32_t h[kHPer];
+  {
+    const uint4* g4 = reinterpret_cast<const uint4*>(g_hist) + tid * (kHPer / 4);
+    uint4 x[kHPer / 4];
+#pragma unroll
+    for (int q = 0; q < kHPer / 4; ++q) x[q] = __ldcg(g4 + q);
+#pragma unroll
+    for (int q = 0; q < kHPer / 4; ++q) {
+      h[4 * q] = x[q].x; h[4 * q + 1] = x[q].y; h[4 * q + 2] = x[q].z; h[4 * q + 3] = x[q].w;
+    }
+  }
+  // The chunk's logits: every thread copies (and later reads) its own 16 B
+  // of each group of 4 * kSThreads entries, one cp.async group per group.
+  // The row buffer is padded to 64 entries, so a float4 that starts below
+  // the row's end stays inside it; past the end the copy zero-fills.
+#pragma unroll
+  for (int u = 0; u < kSPer / 4; ++u) {
+    const int i = t0 + u * 4 * kSThreads + 4 * tid;
+    sm100::cp_async_16(&s.u.vals[u][tid], i < t1 ? row + i : row, i < t1 ? 16u : 0u);
+    sm100::cp_async_commit_group();
+  }
+  if (tid == 0) s.extreme[0] = h[0] != 0u;
+  if (tid == kSThreads - 1) {
+    uint32_t e = 0u;
+#pragma unroll
+    for (int i = kHPer - 8; i < kHPer; ++i) e |= h[i];
+    s.extreme[1] = e != 0u;
+  }
+  find_threshold<kSThreads, kHPer>(s.sc, h, kTopK);  // ends with a barrier
+  const uint32_t bin1 = static_cast<uint32_t>(s.sc.sel_bin);
+  const int above1 = s.sc.sel_above;
+  const int n1 = s.sc.sel_count;
+  const bool listed = n1 <= kSplitCap;
+  const uint32_t key_lo = bin1 << (32 - kHistBits);
+  const uint32_t key_top = key_lo | ((1u << (32 - kHistBits)) - 1u);
+  // A group of 4 logits whose float maximum is below the pivot bin's first
+  // value is skipped after 4 compares (exact for non-NaN values; rows whose
+  // histogram shows NaNs or infinities classify every entry by its key).
+  const bool fast_skip = (s.extreme[0] | s.extreme[1]) == 0;
+  const float f_lo = key_to_float(key_lo);
+
+  uint32_t gtm = 0u, inm = 0u;
+#pragma unroll
+  for (int u = 0; u < kSPer / 4; ++u) {
+    switch (u) {  // this thread's copies of groups 0..u have landed
+      case 0: sm100::cp_async_wait_group<3>(); break;
+      case 1: sm100::cp_async_wait_group<2>(); break;
+      case 2: sm100::cp_async_wait_group<1>(); break;
+      default: sm100::cp_async_wait_group<0>(); break;
+    }
+    const int i0 = t0 + u * 4 * kSThreads + 4 * tid;
+    if (i0 >= t1) continue;
+    const float4 w = s.u.vals[u][tid];
+    if (fast_skip && fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) < f_lo) continue;
+    const uint32_t k4[4] = {key_of_bits(__float_as_uint(w.x)), key_of_bits(__float_as_uint(w.y)),
+                            key_of_bits(__float_as_uint(w.z)), key_of_bits(__float_as_uint(w.w))};
+    uint32_t g = 0u, n = 0u;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      g |= static_cast<uint32_t>(k4[q] > key_top) << q;
+      n |= static_cast<uint32_t>(k4[q] >= key_lo) << q;
+    }
+    const int left = t1 - i0;
+    if (left < 4) {  // entries at or past the row's end
+      const uint32_t valid = (1u << left) - 1u;
+      g &= valid;
+      n &= valid;
+    }
+    gtm |= g << (4 * u);
+    inm |= n << (4 * u);
+  }
+  const uint32_t eqm = listed ? (inm & ~gtm) : 0u;
+
+  // Output and list slots of the chunk: one atomic on the row's counters.
+  uint32_t tot;
+  const uint32_t pre = block_scan_packed<kSThreads>(s.sc, __popc(gtm) | (__popc(eqm) << 16), &tot);
+  if (tid == 0) {
+    const unsigned long long add =
+        (tot & 0xFFFFu) | (static_cast<unsigned long long>(tot >> 16) << 32);
+    const unsigned long long old = add ? atomicAdd(&ctl->slots, add) : 0ull;
+    s.base_out = static_cast<int>(old & 0xFFFFFFFFull);
+    s.base_cand = static_cast<int>(old >> 32);
+  }
+  __syncthreads();
+  auto value_of = [&](int i) -> int32_t {
+    if constexpr (kIds) {
+      return s.bt[(i >> 6) - pg0] * kPage + (i & (kPage - 1));
+    } else {
+      return i;
+    }
+  };
+  {
+    int pos = s.base_out + static_cast<int>(pre & 0xFFFFu);
+    int cpos = s.base_cand + static_cast<int>(pre >> 16);
+    auto entry = [&](int e) { return t0 + (e >> 2) * 4 * kSThreads + 4 * tid + (e & 3); };
+    auto key_of_entry = [&](int e) {
+      return key_of_bits(__float_as_uint(reinterpret_cast<const float*>(&s.u.vals[e >> 2][tid])[e & 3]));
+    };
+    for (uint32_t m = gtm; m; m &= m - 1u) {  // above the pivot bin: straight to the output
+      const int e = __ffs(m) - 1;
+      out.emit(pos++, value_of(entry(e)), kIds ? 0u : key_of_entry(e));
+    }
+    for (uint32_t m = eqm; m; m &= m - 1u) {  // in the pivot bin: to the row's list
+      const int e = __ffs(m) - 1;
+      if (cpos < kSplitCap) {
+        list_key[cpos] = key_of_entry(e);
+        list_val[cpos] = value_of(entry(e));
+      }
+      ++cpos;
+    }
+  }
+
+  // Ticket: the CTA that finishes the row last refines it.  The barrier and
+  // thread 0's fence order the block's output and list writes before its
+  // ticket; the last CTA's fence after the final ticket makes every other
+  // CTA's writes visible to its loads.
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int t = atomicAdd(&ctl->done, 1u);
+    const int last = t == static_cast<unsigned int>(nch - 1);
+    if (last) __threadfence();
+    s.last = last;
+  }
+  __syncthreads();
+  if (!s.last) return;
+
+  // The first kSStage list entries are loaded at once, before their count
+  // is known (one round trip; entries past the count are ignored).
+  constexpr int kStPer = kSStage / kSThreads;
+  uint32_t st_key[kStPer];
+  int32_t st_val[kStPer];
+  if (listed) {
+#pragma unroll
+    for (int q = 0; q < kStPer; ++q) {
+      st_key[q] = __ldcg(list_key + q * kSThreads + tid);
+      st_val[q] = __ldcg(list_val + q * kSThreads + tid);
+    }
+  }
+  if (tid == 0) {
+    const unsigned long long v = __ldcg(&ctl->slots);
+    s.out_count = static_cast<int>(v & 0xFFFFFFFFull);
+    s.n_cand = static_cast<int>(v >> 32);
+    s.small_count = 0;
+    s.eq_count = 0;
+    ctl->slots = 0ull;  // every CTA of the row has taken its slots and ticket
+    ctl->done = 0u;
+  }
+  {
+    // Every CTA of the row has read the histogram: clear it for the next call.
+    uint4* g4 = reinterpret_cast<uint4*>(g_hist) + tid * (kHPer / 4);
+#pragma unroll
+    for (int q = 0; q < kHPer / 4; ++q) g4[q] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  for (int i = tid; i < kBins2; i += kSThreads) s.hist[i] = 0u;
+  if (listed) {
+#pragma unroll
+    for (int q = 0; q < kStPer; ++q) {
+      s.u.list.key[q * kSThreads + tid] = st_key[q];
+      s.u.list.val[q * kSThreads + tid] = st_val[q];
+    }
+  }
+  __syncthreads();
+  const int n3 = listed ? min(s.n_cand, kSplitCap) : L;
+  // Entry j of the pivot bin: from the list (its first kSStage entries
+  // staged in shared memory), or (more keys in the bin than the list keeps)
+  // from the row in global memory, 0 if not in the bin.
+  auto key_at = [&](int j) -> uint32_t {
+    if (listed) return j < kSStage ? s.u.list.key[j] : __ldcg(list_key + j);
+    const uint32_t key = ordered_key(__ldcg(row + j));
+    return (key >> (32 - kHistBits)) == bin1 ? key : 0u;
+  };
+  auto val_at = [&](int j) -> int32_t {
+    if (listed) return j < kSStage ? s.u.list.val[j] : __ldcg(list_val + j);
+    if constexpr (kIds) return physical_id(bt_row, j); else return j;
+  };
+
+  for (int base = 0; base < n3; base += kSThreads) {
+    const int j = base + tid;
+    const uint32_t key = j < n3 ? key_at(j) : 0u;
+    hist_add(s.hist, (key >> 10) & (kBins2 - 1), j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1);
+  }
+  __syncthreads();
+  uint32_t h2[kB2Per];
+#pragma unroll
+  for (int i = 0; i < kB2Per; ++i) h2[i] = s.hist[tid * kB2Per + i];
+  const int k1 = kTopK - above1;
+  find_threshold<kSThreads, kB2Per>(s.sc, h2, k1);
+  const uint32_t prefix2 = (bin1 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k2 = k1 - s.sc.sel_above;  // keys still needed from the second-digit bin
+  const int n2 = s.sc.sel_count;
+
+  if (n2 <= kSSmall) {
+    // Emit the keys above the 22-bit prefix; collect the prefix's keys.
+    for (int base = 0; base < n3; base += kSThreads) {
+      const int j = base + tid;
+      const uint32_t key = j < n3 ? key_at(j) : 0u;
+      const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+      const bool gt = in && (key >> 10) > prefix2;
+      const bool eq = in && (key >> 10) == prefix2;
+      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+      const int q = warp_alloc_n(&s.small_count, eq ? 1 : 0);
+      if (gt) out.emit(pos, val_at(j), key);
+      if (eq && q < kSSmall) {
+        s.small_key[q] = key;
+        s.small_val[q] = val_at(j);
+      }
+    }
+    __syncthreads();
+    // Rank the n2 keys (largest first, ties by list position): key i is
+    // compared with keys 16c..16c+15 by thread 4i + c and the four partial
+    // counts are summed; the k2 best take the last k2 slots.
+    const int n = min(s.small_count, kSSmall);
+    const int i = tid >> 2, c4 = tid & 3;
+    const uint32_t ki = i < n ? s.small_key[i] : 0u;
+    int r = 0;
+#pragma unroll
+    for (int q = 0; q < kSSmall / 4; ++q) {
+      const int j = (kSSmall / 4) * c4 + q;
+      const uint32_t kj = j < n ? s.small_key[j] : 0u;
+      r += (j < n && (kj > ki || (kj == ki && j < i))) ? 1 : 0;
+    }
+    r += __shfl_xor_sync(0xffffffffu, r, 2);
+    r += __shfl_xor_sync(0xffffffffu, r, 1);
+    if (c4 == 0 && i < n && r < k2) out.emit(kTopK - k2 + r, s.small_val[i], ki);
+    return;
+  }
+
+  // Many keys share the 22-bit prefix: count the third digit over them.
+  for (int i = tid; i < kBins2; i += kSThreads) s.hist[i] = 0u;
+  __syncthreads();
+  for (int base = 0; base < n3; base += kSThreads) {
+    const int j = base + tid;
+    const uint32_t key = j < n3 ? key_at(j) : 0u;
+    hist_add(s.hist, key & (kBins2 - 1), j < n3 && key != 0u && (key >> 10) == prefix2);
+  }
+  __syncthreads();
+  uint32_t h3[kB2Per];
+#pragma unroll
+  for (int i = 0; i < kB2Per; ++i) h3[i] = s.hist[tid * kB2Per + i];
+  find_threshold<kSThreads, kB2Per>(s.sc, h3, k2);
+  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+  const int k3 = k2 - s.sc.sel_above;  // how many keys equal to the pivot are taken
+  for (int base = 0; base < n3; base += kSThreads) {
+    const int j = base + tid;
+    const uint32_t key = j < n3 ? key_at(j) : 0u;
+    const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+    const bool gt = in && key > pivot;
+    const bool eq = in && key == pivot;
+    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    if (gt) out.emit(pos, val_at(j), key);
+    if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
+  }
+}
+
 // ------------------------------------------------------------ merge
 
 constexpr int kMThreads = 512;
@@ -1058,6 +1434,21 @@ cudaError_t ensure_attrs() {
                              kWideSmemBytes);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMergeSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSplitSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSplitSmemBytes);
+  // The split kernel's CTAs are small (21 KB): ask for the largest shared
+  // memory carveout so that four of them fit on an SM (the driver may
+  // otherwise size the carveout for fewer).
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_split_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(select_split_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   if (dev >= 0 && dev < 64) g_attr_done[dev] = true;
   return cudaSuccess;
@@ -1097,10 +1488,47 @@ SelectShape select_shape(int rows, int max_pages, int sms) {
   return sh;
 }
 
+// Whether the split kernel (several CTAs per row) may be used; with
+// DSAI_SELECT=rows in the environment (read once) every call uses the
+// one-CTA-per-row / one-cluster-per-row kernels instead (for comparison).
+bool use_split_select() {
+  static const bool split = [] {
+    const char* v = getenv("DSAI_SELECT");
+    return !(v && strcmp(v, "rows") == 0);
+  }();
+  return split;
+}
+
+cudaError_t launch_select_split(const SelectLaunch& p, long long chunks_per_row, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(static_cast<long long>(p.rows) * chunks_per_row));
+  cfg.blockDim = dim3(kSThreads);
+  cfg.dynamicSmemBytes = kSplitSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int cpr = static_cast<int>(chunks_per_row);
+  if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_split_kernel<true>, p, cpr);
+  return cudaLaunchKernelEx(&cfg, select_split_kernel<false>, p, cpr);
+}
+
 cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
   cudaError_t e = ensure_attrs();
   if (e != cudaSuccess) return e;
   if (p.rows <= 0) return cudaSuccess;
+  if (p.cand && use_split_select() && static_cast<long long>(p.rows) * 4 < static_cast<long long>(p.sms)) {
+    // Few rows: several CTAs per row.  (With many rows the one-CTA-per-row
+    // kernel is faster: the split kernel's chain of dependent steps per CTA
+    // — histogram, slot atomic, ticket, refinement — is longer than the wide
+    // CTA's, measured 48.4 against 42.5 us per call at B = 64.)
+    const long long max_len = static_cast<long long>(p.max_pages) * kPage;
+    long long cpr = (max_len + kSChunk - 1) / kSChunk;
+    if (cpr < 1) cpr = 1;
+    if (static_cast<long long>(p.rows) * cpr <= 0x7FFFFFFFll) return launch_select_split(p, cpr, stream);
+  }
   const SelectShape sh = select_shape(p.rows, p.max_pages, p.sms);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.rows) * static_cast<unsigned>(sh.cluster));

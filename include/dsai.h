@@ -95,14 +95,15 @@ typedef struct dsai_args {
 } dsai_args;
 
 /* Bytes of device workspace dsai_run needs for these sizes (256-B aligned
- * base required): a status header, one 4096-bin histogram per row and the
- * fp32 logits.  Replaces the reference's per-device fp16 logits scratch
+ * base required): a status header, per row a 4096-bin histogram with four
+ * counters and an 8192-entry list of (key, id) pairs, and the fp32 logits.
+ * Replaces the reference's per-device fp16 logits scratch
  * (solution/python/kernel.cu:1299-1323).  A workspace serves one call at a
  * time: calls that may overlap on the GPU need separate workspaces. */
 DSAI_API size_t dsai_workspace_size(int32_t rows, int32_t max_pages);
 
-/* Zero a workspace (status word and histograms).  Call once after
- * allocating it; every call leaves the histograms zero again, and the status
+/* Zero a workspace (status word, histograms and counters).  Call once after
+ * allocating it; every call leaves them zero again, and the status
  * word is sticky until dsai_read_status. */
 DSAI_API int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 

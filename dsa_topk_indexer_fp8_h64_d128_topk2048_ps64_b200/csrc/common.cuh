@@ -38,7 +38,7 @@ constexpr int kHistBins = 1 << kHistBits;
 // taken, chunks finished).  They are zero between calls like the bins.
 constexpr int kHistStride = kHistBins + 4;
 // Pivot-bin keys the split selection keeps per row (workspace lists).
-constexpr int kSplitCap = 8192;
+constexpr int kSplitCap = 4096;
 
 constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s bound on any on-chip wait
 

@@ -107,12 +107,25 @@ __device__ __forceinline__ int warp_alloc_n(int* counter, int cnt) {
   return base + incl - cnt;
 }
 
+// The same for a 0/1 flag per lane (a ballot instead of the scan): returns
+// this lane's slot, meaningful where flag is set.
+__device__ __forceinline__ int warp_alloc_1(int* counter, bool flag) {
+  const unsigned m = __ballot_sync(0xffffffffu, flag);
+  const int lane = threadIdx.x & 31;
+  const int leader = m ? __ffs(m) - 1 : 0;
+  int base = 0;
+  if (m && lane == leader) base = atomicAdd(counter, __popc(m));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  return base + __popc(m & ((1u << lane) - 1u));
+}
+
 // Finds the bin holding the k-th largest entry of a histogram spread over
 // the block (thread t holds bins [t*PER, t*PER + PER) in h): sets sel_bin
 // to the bin with above(bin) < k <= above(bin) + count(bin), sel_above to
 // above(bin) (entries in higher bins) and sel_count to count(bin); all zero
 // if the histogram holds fewer than k entries.  A two-level shuffle suffix
-// scan (lanes, then the warp totals).  Ends with a block barrier.
+// scan (lanes, then the warp totals, summed by every warp).  Ends with a
+// block barrier.
 template <int NT, int PER>
 __device__ void find_threshold(Scan& sc, const uint32_t (&h)[PER], int k) {
   constexpr int kW = NT / 32;
@@ -133,17 +146,12 @@ __device__ void find_threshold(Scan& sc, const uint32_t (&h)[PER], int k) {
     sc.sel_count = 0;
   }
   __syncthreads();
-  if (warp == 0) {
-    int t = lane < kW ? sc.warp_tot[lane] : 0;
+  // Entries in the warps above this one: every warp sums the totals itself
+  // (one barrier fewer than a scan by one warp).
+  int t = (lane > warp && lane < kW) ? sc.warp_tot[lane] : 0;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int y = __shfl_down_sync(0xffffffffu, t, off);
-      if (lane + off < 32) t += y;
-    }
-    sc.warp_suf[lane] = t;  // entries in warps >= lane
-  }
-  __syncthreads();
-  int above = (warp < kW - 1 ? sc.warp_suf[warp + 1] : 0) + (v - sum);
+  for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  int above = t + (v - sum);
 #pragma unroll
   for (int i = PER - 1; i >= 0; --i) {
     const int hi = static_cast<int>(h[i]);
@@ -568,8 +576,8 @@ __global__ void __launch_bounds__(NT, SelShape<NT>::kCtasPerSm) select_rows_kern
       const bool in_bin = j < n3 && (key >> (32 - kHistBits)) == bin1;
       const bool gt = in_bin && key > pivot;
       const bool eq = in_bin && key == pivot;
-      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-      const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+      const int pos = warp_alloc_1(&s.out_count, gt);
+      const int ticket = warp_alloc_1(&s.eq_count, eq);
       if (gt || (eq && ticket < k3)) {
         int32_t val;
         if (listed) {
@@ -624,7 +632,7 @@ static_assert(kCPer / 4 == 8, "eight cp.async groups per round");
 // in the pass (output and candidate slots come from one shared atomic per
 // warp).  After the pass, the second digit is found from the histogram the
 // pass built; the few keys sharing the 22-bit prefix (at most 64, else a
-// third digit is counted) are ranked by one warp.
+// third digit is counted) are ranked by the block.
 template <bool kIds>
 __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectLaunch p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -828,8 +836,8 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
       const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
       const bool gt = in && (key >> 10) > prefix2;
       const bool eq = in && (key >> 10) == prefix2;
-      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-      const int q = warp_alloc_n(&s.small_count, eq ? 1 : 0);
+      const int pos = warp_alloc_1(&s.out_count, gt);
+      const int q = warp_alloc_1(&s.small_count, eq);
       if (gt) out.emit(pos, val_at(j), key);
       if (eq && q < kSmall) {
         s.small_key[q] = key;
@@ -866,7 +874,7 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
   for (int base = 0; base < n3; base += kWThreads) {
     const int j = base + tid;
     const uint32_t key = j < n3 ? key_at(j) : 0u;
-    hist_add(s.hist, key & (kBins2 - 1), j < n3 && key != 0u && (key >> 10) == prefix2);
+    if (j < n3 && key != 0u && (key >> 10) == prefix2) atomicAdd(&s.hist[key & (kBins2 - 1)], 1u);
   }
   __syncthreads();
   uint32_t h3[1] = {s.hist[tid]};
@@ -879,8 +887,8 @@ __global__ void __launch_bounds__(kWThreads, 1) select_wide_kernel(const SelectL
     const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
     const bool gt = in && key > pivot;
     const bool eq = in && key == pivot;
-    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    const int pos = warp_alloc_1(&s.out_count, gt);
+    const int ticket = warp_alloc_1(&s.eq_count, eq);
     if (gt) out.emit(pos, val_at(j), key);
     if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
   }
@@ -1178,7 +1186,7 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
   for (int base = 0; base < n3; base += kSThreads) {
     const int j = base + tid;
     const uint32_t key = j < n3 ? key_at(j) : 0u;
-    hist_add(s.hist, (key >> 10) & (kBins2 - 1), j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1);
+    if (j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1) atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
   }
   __syncthreads();
   uint32_t h2[kB2Per];
@@ -1198,8 +1206,8 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
       const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
       const bool gt = in && (key >> 10) > prefix2;
       const bool eq = in && (key >> 10) == prefix2;
-      const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-      const int q = warp_alloc_n(&s.small_count, eq ? 1 : 0);
+      const int pos = warp_alloc_1(&s.out_count, gt);
+      const int q = warp_alloc_1(&s.small_count, eq);
       if (gt) out.emit(pos, val_at(j), key);
       if (eq && q < kSSmall) {
         s.small_key[q] = key;
@@ -1232,7 +1240,7 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
   for (int base = 0; base < n3; base += kSThreads) {
     const int j = base + tid;
     const uint32_t key = j < n3 ? key_at(j) : 0u;
-    hist_add(s.hist, key & (kBins2 - 1), j < n3 && key != 0u && (key >> 10) == prefix2);
+    if (j < n3 && key != 0u && (key >> 10) == prefix2) atomicAdd(&s.hist[key & (kBins2 - 1)], 1u);
   }
   __syncthreads();
   uint32_t h3[kB2Per];
@@ -1247,8 +1255,8 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
     const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
     const bool gt = in && key > pivot;
     const bool eq = in && key == pivot;
-    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
-    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    const int pos = warp_alloc_1(&s.out_count, gt);
+    const int ticket = warp_alloc_1(&s.eq_count, eq);
     if (gt) out.emit(pos, val_at(j), key);
     if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
   }
@@ -1320,9 +1328,9 @@ __global__ void __launch_bounds__(kMThreads, 1)
     const uint32_t bb = key >> (32 - kHistBits);
     const bool gt = key != 0u && bb > bin1;
     const bool eq = use_cand && key != 0u && bb == bin1;
-    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    const int pos = warp_alloc_1(&s.out_count, gt);
     if (gt && pos < kTopK) out[pos] = physical_id(bt_row, tokens[i]);
-    const int cpos = warp_alloc_n(&s.cand_count, eq ? 1 : 0);
+    const int cpos = warp_alloc_1(&s.cand_count, eq);
     if (eq && cpos < kCandCap) {
       s.cand_key[cpos] = key;
       s.cand_idx[cpos] = i;
@@ -1370,9 +1378,9 @@ __global__ void __launch_bounds__(kMThreads, 1)
     const uint32_t key = bucket(j);
     const bool gt = key != 0u && key > pivot;
     const bool eq = key != 0u && key == pivot;
-    const int pos = warp_alloc_n(&s.out_count, gt ? 1 : 0);
+    const int pos = warp_alloc_1(&s.out_count, gt);
     if (gt && pos < kTopK) out[pos] = physical_id(bt_row, tokens[index_of(j)]);
-    const int ticket = warp_alloc_n(&s.eq_count, eq ? 1 : 0);
+    const int ticket = warp_alloc_1(&s.eq_count, eq);
     const int slot = kTopK - k3 + ticket;
     if (eq && ticket < k3 && slot >= 0 && slot < kTopK) out[slot] = physical_id(bt_row, tokens[index_of(j)]);
   }

@@ -96,7 +96,7 @@ typedef struct dsai_args {
 
 /* Bytes of device workspace dsai_run needs for these sizes (256-B aligned
  * base required): a status header, per row a 4096-bin histogram with four
- * counters and an 8192-entry list of (key, id) pairs, and the fp32 logits.
+ * counters and a 4096-entry list of (key, id) pairs, and the fp32 logits.
  * Replaces the reference's per-device fp16 logits scratch
  * (solution/python/kernel.cu:1299-1323).  A workspace serves one call at a
  * time: calls that may overlap on the GPU need separate workspaces. */

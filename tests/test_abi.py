@@ -40,12 +40,12 @@ def test_only_the_api_is_exported(dsai_lib):
 
 def test_workspace_size(dsai_lib):
     # header + per row a 4096-bin u32 histogram with 4 u32 counters (256-B
-    # rounded) + per row an 8192-entry (key, value) list + fp32 logits (256-B rounded)
+    # rounded) + per row a 4096-entry (key, value) list + fp32 logits (256-B rounded)
     def r256(n):
         return (n + 255) // 256 * 256
     assert dsai_lib.dsai_workspace_size(0, 0) == 256
-    assert dsai_lib.dsai_workspace_size(64, 512) == 256 + r256(64 * 16400) + 64 * 65536 + 64 * 512 * 64 * 4
-    assert dsai_lib.dsai_workspace_size(3, 5) == 256 + r256(3 * 16400) + 3 * 65536 + r256(3 * 5 * 64 * 4)
+    assert dsai_lib.dsai_workspace_size(64, 512) == 256 + r256(64 * 16400) + 64 * 32768 + 64 * 512 * 64 * 4
+    assert dsai_lib.dsai_workspace_size(3, 5) == 256 + r256(3 * 16400) + 3 * 32768 + r256(3 * 5 * 64 * 4)
     assert dsai_lib.dsai_workspace_size(-1, 4) == 0
 
 

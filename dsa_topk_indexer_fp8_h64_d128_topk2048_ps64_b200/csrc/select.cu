@@ -1297,6 +1297,23 @@ __global__ void __launch_bounds__(kMThreads, 1)
     for (int i = tid; i < kTopK; i += kMThreads) out[i] = i < L ? physical_id(bt_row, i) : -1;
     return;
   }
+  if (n <= kTopK) {
+    // No more candidates than output slots (one rank's list): every real
+    // one is selected; compacted in shared memory, then all slots written.
+    if (tid == 0) s.out_count = 0;
+    __syncthreads();
+    for (int base = 0; base < n; base += kMThreads) {
+      const int i = base + tid;
+      const int t = i < n ? tokens[i] : -1;
+      const bool real = t >= 0 && t < L;
+      const int pos = warp_alloc_1(&s.out_count, real);
+      if (real) s.cand_idx[pos] = physical_id(bt_row, t);
+    }
+    __syncthreads();
+    const int cnt = s.out_count;
+    for (int i = tid; i < kTopK; i += kMThreads) out[i] = i < cnt ? s.cand_idx[i] : -1;
+    return;
+  }
   // Slots stay -1 if the lists hold fewer than kTopK real entries.
   for (int i = tid; i < kTopK; i += kMThreads) out[i] = -1;
   for (int i = tid; i < kHistBins; i += kMThreads) s.hist[i] = 0u;

@@ -37,7 +37,7 @@ def emulated_split(g, world):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_config3_split_matches_direct_and_oracle(oracle_mod, world):
     inp = W.config_inputs(3)          # B=1, L=131072, 16 planted tokens
     g = inp.to(DEV)
@@ -81,3 +81,26 @@ def test_pairs_short_rows_and_offsets(oracle_mod):
     ora = oracle_mod.logits(d["q"], d["k_cache"], d["weights"], d["seq_lens"], d["block_table"])
     osc, otk = oracle_mod.pairs(ora, d["seq_lens"], 1000)
     assert set(tk[1].tolist()) == set(otk[1].tolist())
+
+
+def test_merge_list_no_longer_than_topk():
+    """A candidate list of at most 2048 entries (one rank's pairs): every real
+    entry is selected, padding (-1) and tokens past the row are not."""
+    inp = W.make_inputs([6000], seed=31)
+    g = inp.to(DEV)
+    gen = torch.Generator().manual_seed(31)
+    tokens = torch.randperm(6000, generator=gen)[:2048].to(torch.int32)
+    tokens[::7] = -1          # padding
+    tokens[3::11] = 7000      # past the row's end
+    scores = torch.randn(2048, generator=gen)
+    out = torch.empty(TOPK, dtype=torch.int32, device=DEV)
+    merge_pairs(scores.to(DEV), tokens.to(DEV), g.block_table[0].contiguous(), g.seq_lens[:1].contiguous(), out)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    bt = inp.block_table[0].numpy()
+    real = tokens.numpy()
+    real = real[(real >= 0) & (real < 6000)]
+    expect = bt[real // 64] * 64 + real % 64
+    n = len(expect)
+    assert np.array_equal(np.sort(got[:n]), np.sort(expect))
+    assert np.all(got[n:] == -1)

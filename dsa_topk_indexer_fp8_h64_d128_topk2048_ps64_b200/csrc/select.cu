@@ -1265,8 +1265,10 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
 // ------------------------------------------------------------ merge
 
 constexpr int kMThreads = 512;
+constexpr int kMergeStage = 16384;  // candidate keys staged in shared memory (8 ranks' lists)
 
 struct MergeSmem {
+  uint32_t key_all[kMergeStage];
   uint32_t hist[kHistBins];
   uint32_t cand_key[kCandCap];
   int32_t cand_idx[kCandCap];
@@ -1283,7 +1285,8 @@ constexpr int kMergeSmemBytes = static_cast<int>(sizeof(MergeSmem));
 // of one NaN bit pattern only).
 __device__ __forceinline__ uint32_t cand_key_of(const float* scores, const int32_t* tokens, int L, int i) {
   const int t = tokens[i];
-  return (t >= 0 && t < L) ? ordered_key(scores[i]) : 0u;
+  const float x = scores[i];  // loaded with the token, not after it
+  return (t >= 0 && t < L) ? ordered_key(x) : 0u;
 }
 
 __global__ void __launch_bounds__(kMThreads, 1)
@@ -1322,10 +1325,29 @@ __global__ void __launch_bounds__(kMThreads, 1)
     s.cand_count = 0;
     s.eq_count = 0;
   }
+  // The candidates' keys go to shared memory once, eight loads in flight per
+  // thread, and every later pass reads them there (up to 8 ranks' lists).
+  const bool staged = n <= kMergeStage;
+  if (staged) {
+    for (int base = 0; base < n; base += 8 * kMThreads) {
+      uint32_t k[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int i = base + q * kMThreads + tid;
+        k[q] = i < n ? cand_key_of(scores, tokens, L, i) : 0u;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int i = base + q * kMThreads + tid;
+        if (i < n) s.key_all[i] = k[q];
+      }
+    }
+  }
+  auto key_of = [&](int i) -> uint32_t { return staged ? s.key_all[i] : cand_key_of(scores, tokens, L, i); };
   __syncthreads();
   for (int base = 0; base < n; base += kMThreads) {
     const int i = base + tid;
-    const uint32_t key = i < n ? cand_key_of(scores, tokens, L, i) : 0u;
+    const uint32_t key = i < n ? key_of(i) : 0u;
     hist_add(s.hist, key >> (32 - kHistBits), key != 0u);
   }
   __syncthreads();
@@ -1341,7 +1363,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
   // Emit keys above the pivot bin; collect the pivot bin.
   for (int base = 0; base < n; base += kMThreads) {
     const int i = base + tid;
-    const uint32_t key = i < n ? cand_key_of(scores, tokens, L, i) : 0u;
+    const uint32_t key = i < n ? key_of(i) : 0u;
     const uint32_t bb = key >> (32 - kHistBits);
     const bool gt = key != 0u && bb > bin1;
     const bool eq = use_cand && key != 0u && bb == bin1;
@@ -1358,7 +1380,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
   auto bucket = [&](int j) -> uint32_t {  // key of the j-th pivot-bin entry, or 0
     if (j >= m) return 0u;
     if (use_cand) return s.cand_key[j];
-    const uint32_t key = cand_key_of(scores, tokens, L, j);
+    const uint32_t key = key_of(j);
     return (key >> (32 - kHistBits)) == bin1 ? key : 0u;
   };
   auto index_of = [&](int j) { return use_cand ? s.cand_idx[j] : j; };
@@ -1367,7 +1389,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
   __syncthreads();
   for (int base = 0; base < m; base += kMThreads) {
     const uint32_t key = bucket(base + tid);
-    hist_add(s.hist, (key >> 10) & (kBins2 - 1), key != 0u);
+    if (key != 0u) atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
   }
   __syncthreads();
   uint32_t h2[kPer2];
@@ -1381,7 +1403,7 @@ __global__ void __launch_bounds__(kMThreads, 1)
   __syncthreads();
   for (int base = 0; base < m; base += kMThreads) {
     const uint32_t key = bucket(base + tid);
-    hist_add(s.hist, key & (kBins2 - 1), key != 0u && (key >> 10) == prefix2);
+    if (key != 0u && (key >> 10) == prefix2) atomicAdd(&s.hist[key & (kBins2 - 1)], 1u);
   }
   __syncthreads();
 #pragma unroll

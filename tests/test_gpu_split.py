@@ -37,7 +37,7 @@ def emulated_split(g, world):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("world", [1, 2, 4, 8, 16])
 def test_config3_split_matches_direct_and_oracle(oracle_mod, world):
     inp = W.config_inputs(3)          # B=1, L=131072, 16 planted tokens
     g = inp.to(DEV)

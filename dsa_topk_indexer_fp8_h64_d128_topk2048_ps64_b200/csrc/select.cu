@@ -950,6 +950,7 @@ struct SplitSmem {
 constexpr int kSplitSmemBytes = static_cast<int>(sizeof(SplitSmem));
 static_assert(sizeof(SplitSmem::u) == kSPer / 4 * kSThreads * 16, "the list staging reuses the logits buffer");
 static_assert(kSStage % kSThreads == 0, "list staging");
+static_assert(kSplitCap / kSThreads <= 32, "a 32-bit mask of list entries per thread");
 static_assert(kSThreads == 4 * kSSmall, "four threads rank each of the 64 keys");
 
 template <bool kIds>
@@ -1200,18 +1201,47 @@ __global__ void __launch_bounds__(kSThreads, 4) select_split_kernel(const Select
 
   if (n2 <= kSSmall) {
     // Emit the keys above the 22-bit prefix; collect the prefix's keys.
-    for (int base = 0; base < n3; base += kSThreads) {
-      const int j = base + tid;
-      const uint32_t key = j < n3 ? key_at(j) : 0u;
-      const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
-      const bool gt = in && (key >> 10) > prefix2;
-      const bool eq = in && (key >> 10) == prefix2;
-      const int pos = warp_alloc_1(&s.out_count, gt);
-      const int q = warp_alloc_1(&s.small_count, eq);
-      if (gt) out.emit(pos, val_at(j), key);
-      if (eq && q < kSSmall) {
-        s.small_key[q] = key;
-        s.small_val[q] = val_at(j);
+    if (listed) {
+      // Every thread classifies all its list entries (j = tid + 256q) first,
+      // then takes its output and small-list slots with one allocation each
+      // (not one pair per 256 entries).
+      constexpr int kLPer = kSplitCap / kSThreads;
+      uint32_t gtb = 0u, eqb = 0u;
+#pragma unroll
+      for (int q = 0; q < kLPer; ++q) {
+        const int j = q * kSThreads + tid;
+        const uint32_t key = j < n3 ? key_at(j) : 0u;
+        const bool in = key != 0u && (key >> (32 - kHistBits)) == bin1;
+        gtb |= static_cast<uint32_t>(in && (key >> 10) > prefix2) << q;
+        eqb |= static_cast<uint32_t>(in && (key >> 10) == prefix2) << q;
+      }
+      int pos = warp_alloc_n(&s.out_count, __popc(gtb));
+      int qs = warp_alloc_n(&s.small_count, __popc(eqb));
+      for (uint32_t m = gtb; m; m &= m - 1u) {
+        const int j = (__ffs(m) - 1) * kSThreads + tid;
+        out.emit(pos++, val_at(j), key_at(j));
+      }
+      for (uint32_t m = eqb; m; m &= m - 1u, ++qs) {
+        const int j = (__ffs(m) - 1) * kSThreads + tid;
+        if (qs < kSSmall) {
+          s.small_key[qs] = key_at(j);
+          s.small_val[qs] = val_at(j);
+        }
+      }
+    } else {
+      for (int base = 0; base < n3; base += kSThreads) {
+        const int j = base + tid;
+        const uint32_t key = j < n3 ? key_at(j) : 0u;
+        const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+        const bool gt = in && (key >> 10) > prefix2;
+        const bool eq = in && (key >> 10) == prefix2;
+        const int pos = warp_alloc_1(&s.out_count, gt);
+        const int q = warp_alloc_1(&s.small_count, eq);
+        if (gt) out.emit(pos, val_at(j), key);
+        if (eq && q < kSSmall) {
+          s.small_key[q] = key;
+          s.small_val[q] = val_at(j);
+        }
       }
     }
     __syncthreads();

@@ -207,11 +207,10 @@ __global__ void __launch_bounds__(MqTraits<R>::kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // Launched as a programmatic dependent: nothing before this point touches
-  // global memory, so the launch overlaps the previous kernel's tail.
-  sm100::grid_dep_wait();
-  sm100::grid_dep_launch_dependents();
-  build_group_table(s, p);
+  // Launched as a programmatic dependent: the barriers and the tensor-map
+  // prefetch (shared memory and kernel parameters only) overlap the previous
+  // kernel's tail; global memory is touched only after the wait.  (TMEM is
+  // allocated after it: a predecessor still running on this SM may need it.)
   if (tid == 0) {
     for (int i = 0; i < kMqStages; ++i) {
       mbar_init(&s.full[i], 1);
@@ -240,6 +239,9 @@ __global__ void __launch_bounds__(MqTraits<R>::kThreads, 1)
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_s);
   }
+  sm100::grid_dep_wait();
+  sm100::grid_dep_launch_dependents();
+  build_group_table(s, p);
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, kMqTmemCols);
     tmem_relinquish();

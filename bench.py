@@ -55,13 +55,39 @@ from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import workloads as W  # n
 
 METRIC = "index-K HBM GB/s per indexer call (score + top-2048), B=64 decode"
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one score_kernel launch, from one ncu capture
-# of this bench's workload (dram__bytes_read.sum + dram__bytes_write.sum;
-# summary and command in profiles/score_kernel_config1.md).  Other configs
-# have no capture: their traffic is reported as null.
-SCORE_TRAFFIC_BYTES = {1: 156_324_096 + 4_711_168, 4: 156_743_680 + 6_461_696}
-SCORE_PROFILE = {1: "score_kernel_config1.md", 4: "score_mq_kernel_config4.md"}
+# DRAM bytes (read + write) of one scoring launch from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of this bench's workload,
+# with the SHA-256 of the kernel sources that capture ran.  roofline.traffic
+# reports it only while the sources still hash the same; otherwise it is
+# null and the old capture is shown as traffic_last_profiled.
+SCORE_TRAFFIC = {
+    1: {"bytes": 156_324_096 + 4_711_168, "src_sha256": "", "kernel": "score_kernel"},
+    4: {"bytes": 156_743_680 + 6_461_696, "src_sha256": "", "kernel": "score_mq_kernel<4>"},
+}
 N_SETS = 3
+
+
+def kernel_sources_sha256() -> str:
+    """SHA-256 over the CUDA sources and headers the library is built from."""
+    import hashlib
+    h = hashlib.sha256()
+    csrc = REPO / "dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200" / "csrc"
+    for f in sorted(list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh")) + list(csrc.glob("*.h"))):
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    h.update((REPO / "include" / "dsai.h").read_bytes())
+    return h.hexdigest()
+
+
+def traffic_entry(config: int, rows_per_seq: int, config_rps: int) -> dict:
+    cap = SCORE_TRAFFIC.get(config)
+    if cap is None or rows_per_seq != config_rps:
+        return {"traffic": None, "traffic_source": "no ncu capture for this workload"}
+    if cap["src_sha256"] and cap["src_sha256"] == kernel_sources_sha256():
+        return {"traffic": cap["bytes"],
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of this build"}
+    return {"traffic": None, "traffic_last_profiled": cap["bytes"],
+            "traffic_source": "the last ncu capture ran other kernel sources; not reported as this build's"}
 
 
 def measured_hbm_peak():
@@ -227,6 +253,38 @@ def cpu_oracle_sample(inp_cpu: W.Inputs, budget_s: float):
     return sub.algorithmic_bytes() / dt / 1e9, n, dt, threads
 
 
+def time_reference_kernel(sets, steps: int, warmup: int) -> dict:
+    """The reference's own CUDA kernel (solution/cuda/kernel.cu, built
+    unmodified by baseline/Makefile) on the same rotating input sets: K
+    back-to-back calls through its entry point, CUDA events on the current
+    stream.  Its stage 1 writes fp16 logits into a scratch it allocates per
+    call through torch (solution/cuda/kernel.cu:471-476)."""
+    from baseline import ref_kernel
+    ok, why = ref_kernel.available()
+    if not ok:
+        return {"unavailable": why}
+    outs = [s.out() for s in sets]
+
+    def step(i):
+        s = sets[i % len(sets)]
+        ref_kernel.kernel(s.q, s.k_cache, s.weights, s.seq_lens, s.block_table, outs[i % len(sets)])
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    alg = sets[0].algorithmic_bytes()
+    return {"source": ref_kernel.SOURCE, "us_per_call": round(ms * 1e3, 2),
+            "value": round(alg / (ms / 1e3) / 1e9, 1), "unit": "GB/s", "steps": steps,
+            "timing": "CUDA events over back-to-back calls through its TVM-FFI entry point"}
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -390,12 +448,7 @@ def bench_ours(args, world, rank, local):
     kname = "score_kernel" if R == 1 else f"score_mq_kernel<{R}>"
     roof = {"kernel": kname, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
             "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / peak, 4),
-            "algorithmic_bytes_per_launch": sbytes,
-            "traffic": SCORE_TRAFFIC_BYTES.get(args.config) if R == config_rps else None,
-            "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch "
-                               f"(profiles/{SCORE_PROFILE.get(args.config, '')})"
-                               if args.config in SCORE_TRAFFIC_BYTES and R == config_rps
-                               else "no ncu capture for this config")}
+            "algorithmic_bytes_per_launch": sbytes, **traffic_entry(args.config, R, config_rps)}
     flops = score_flops(base)
     tpeak, tpeak_src = measured_fp8_peak()
     tensor = {"achieved": round(flops / (score_ms / 1e3) / 1e12, 1), "peak": round(tpeak, 1),
@@ -435,6 +488,8 @@ def bench_ours(args, world, rank, local):
         "gpu_launches": 2 * args.steps,
         "clocks": clk,
     }
+    if world == 1 and R == 1 and not args.no_reference_kernel:
+        line["reference_kernel"] = time_reference_kernel(sets, max(3, min(args.steps, 200)), args.warmup)
     if world == 1 and not args.no_cpu_baseline:
         gbs, n, dt, threads = cpu_oracle_sample(base.to("cpu"), args.cpu_budget)
         line["cpu_baseline"] = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -731,9 +786,9 @@ def bench_attn(args, world, rank, local):
         "roofline": {"kernel": "attn_kernel (+ attn_combine_kernel)", "bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peak, "peak_source": peak_src, "unit": "GB/s", "frac": round(gbs / peak, 4),
                      "algorithmic_bytes_per_launch": alg,
-                     "traffic": 152_770_560 + 4_194_048 if T == 64 else None,
-                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of attn_kernel, one launch "
-                                        "(profiles/attn_kernel_t64.md)" if T == 64 else "no ncu capture for this size"),
+                     "traffic": None,
+                     "traffic_last_profiled": 152_770_560 + 4_194_048 if T == 64 else None,
+                     "traffic_source": "ncu capture of an earlier build of attn_kernel (T=64), not of this run",
                      "tensor": {"achieved": round(flops / (us / 1e6) / 1e12, 1), "unit": "TFLOP/s",
                                 "algorithmic_flops_per_launch": flops}},
         "gpu_launches": 2 * args.steps,
@@ -815,6 +870,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU oracle work for cpu_baseline")
     ap.add_argument("--ref-step-budget", type=float, default=2.0, help="seconds per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference-kernel", action="store_true",
+                    help="skip timing the reference's own CUDA kernel (reference_kernel key)")
     ap.add_argument("--chunk", type=int, default=256, help="--op prefill: query rows of the chunk")
     ap.add_argument("--last-len", type=int, default=65536, help="--op prefill: tokens the last row sees")
     ap.add_argument("--tokens-attn", type=int, default=64, help="--op attn: decode tokens per call")

@@ -40,7 +40,7 @@ E_UNSUPPORTED = -4
 EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
     "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
-    "dsai_run_noalloc", "dsai_selftest_wait_timeout", "dsai_write_k",
+    "dsai_run_noalloc", "dsai_noalloc_read_status", "dsai_selftest_wait_timeout", "dsai_write_k",
     "dsai_sparse_attn_workspace_size", "dsai_sparse_attn",
 )
 
@@ -109,6 +109,8 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.dsai_merge_pairs.restype = ctypes.c_int
         lib.dsai_run_noalloc.argtypes = [ctypes.POINTER(DsaiArgs), vp]
         lib.dsai_run_noalloc.restype = ctypes.c_int
+        lib.dsai_noalloc_read_status.argtypes = [vp, ctypes.POINTER(i32)]
+        lib.dsai_noalloc_read_status.restype = ctypes.c_int
         lib.dsai_selftest_wait_timeout.argtypes = [vp, ctypes.c_uint64, vp]
         lib.dsai_selftest_wait_timeout.restype = ctypes.c_int
         lib.dsai_write_k.argtypes = [vp, i32, vp, i32, vp, i32, vp]
@@ -138,8 +140,9 @@ def workspace_size(rows: int, max_pages: int) -> int:
 
 
 class Workspace:
-    """A device workspace for dsai_run, grown on demand (one per device and
-    stream user).  Its header holds the sticky device status word."""
+    """A device workspace for dsai_run, grown on demand.  Use one per
+    stream: two calls in flight on one workspace at once corrupt each
+    other.  Its header holds the sticky device status word."""
 
     def __init__(self, device: torch.device):
         self.device = torch.device(device)
@@ -164,14 +167,27 @@ class Workspace:
         return int(out.value)
 
 
-_workspaces: dict[int, Workspace] = {}
+_workspaces: dict[tuple[int, int], Workspace] = {}
+_workspaces_lock = threading.Lock()
 
 
-def default_workspace(device: torch.device) -> Workspace:
+def default_workspace(device: torch.device, stream: int | None = None) -> Workspace:
+    """The workspace that ``kernel()`` / ``run()`` use on `device` when
+    called on `stream` (a raw ``cudaStream_t`` value; None = the device's
+    current torch stream).  One workspace per (device, stream): calls
+    issued on different streams may overlap on the GPU, and a shared
+    workspace would let them overwrite each other's histograms, counters
+    and logits.  Calls on one stream are ordered, so they share one."""
     idx = torch.device(device).index
     if idx is None:
         idx = torch.cuda.current_device()
-    ws = _workspaces.get(idx)
+    if stream is None:
+        stream = torch.cuda.current_stream(idx).cuda_stream
+    key = (idx, int(stream))
+    ws = _workspaces.get(key)
     if ws is None:
-        ws = _workspaces[idx] = Workspace(torch.device("cuda", idx))
+        with _workspaces_lock:
+            ws = _workspaces.get(key)
+            if ws is None:
+                ws = _workspaces[key] = Workspace(torch.device("cuda", idx))
     return ws

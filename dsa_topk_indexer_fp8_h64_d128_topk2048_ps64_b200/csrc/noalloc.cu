@@ -56,6 +56,8 @@ int noalloc_setup(int dev, cudaStream_t stream, void** out) {
 
 extern "C" int dsai_run_noalloc(const dsai_args* args, void* stream_) {
   if (!args) return dsai::set_last_error(DSAI_E_INVALID, "args is NULL");
+  if (args->rows < 0 || args->max_pages < 0 || args->num_pages < 0)
+    return dsai::set_last_error(DSAI_E_INVALID, "negative size");
   const size_t need = dsai_workspace_size(args->rows, args->max_pages);
   if (need == 0 || need > kNoAllocScratchBytes) {
     char msg[160];
@@ -72,4 +74,21 @@ extern "C" int dsai_run_noalloc(const dsai_args* args, void* stream_) {
   const int rc = noalloc_setup(dev, stream, &ws);
   if (rc != DSAI_OK) return rc;
   return dsai_run(args, ws, kNoAllocScratchBytes, stream_);
+}
+
+extern "C" int dsai_noalloc_read_status(void* stream, int32_t* status_out) {
+  if (!status_out) return dsai::set_last_error(DSAI_E_INVALID, "status_out is NULL");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return dsai::set_last_error(DSAI_E_CUDA, "no current CUDA device");
+  void* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    ws = g_noalloc_ptr[dev];
+  }
+  if (ws == nullptr) {  // no call on this device yet: nothing to report
+    *status_out = 0;
+    return DSAI_OK;
+  }
+  return dsai_read_status(ws, stream, status_out);
 }

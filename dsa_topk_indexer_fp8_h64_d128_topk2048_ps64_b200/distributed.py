@@ -8,7 +8,8 @@ NVLink/NVSwitch), used only where the indexer shards naturally.
 * One very long row (a single long request) is split by page range:
   ``split_row_topk`` scores the rank's pages as a sub-row, selects its local
   top-2048 as (fp32 score, global token) pairs, exchanges the 2048 pairs of
-  every rank with one all-gather (16 KB per rank) and merges them into the
+  every rank with one all-gather (scores and tokens packed together, 16 KB
+  per rank) and merges them into the
   row's top-2048 physical ids with the full block table.
 
 The reference is single-GPU; this layer has no counterpart there.  The local
@@ -89,11 +90,14 @@ def split_row_topk(q_row, k_cache_local, weights_row, seq_len: int, bt_local_row
     merge = merge or _cuda_merge
     sc, tk = local_pairs(q_row, k_cache_local, weights_row, local_len, bt_local, p0 * PAGE_SIZE)
     if world > 1:
-        all_sc = [torch.empty_like(sc) for _ in range(world)]
-        all_tk = [torch.empty_like(tk) for _ in range(world)]
-        dist.all_gather(all_sc, sc.contiguous(), group=group)
-        dist.all_gather(all_tk, tk.contiguous(), group=group)
-        sc, tk = torch.cat(all_sc), torch.cat(all_tk)
+        # one collective: the scores' fp32 bits and the tokens packed as
+        # int32 [2, 2048] (16 KB per rank)
+        packed = torch.stack([sc.contiguous().view(torch.int32), tk.contiguous()])
+        bufs = [torch.empty_like(packed) for _ in range(world)]
+        dist.all_gather(bufs, packed, group=group)
+        allp = torch.stack(bufs)                     # [world, 2, 2048]
+        sc = allp[:, 0].reshape(-1).contiguous().view(torch.float32)
+        tk = allp[:, 1].reshape(-1).contiguous()
     merge(sc, tk, bt_full_row, seq_len, out)
     return out
 

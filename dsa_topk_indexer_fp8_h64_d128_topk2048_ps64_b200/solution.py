@@ -101,7 +101,7 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
              "logits_out must be float32 contiguous CUDA [B, max_pages*64]")
     dev = block_table.device
     stream = torch.cuda.current_stream(dev).cuda_stream
-    ws = workspace or _lib.default_workspace(dev)
+    ws = workspace or _lib.default_workspace(dev, stream)
     ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
     a = _args(q_index_fp8 if needs_scoring else None, k_index_cache_fp8 if needs_scoring else None,
               weights if needs_scoring else None, seq_lens, block_table, topk_indices, logits_out,
@@ -139,7 +139,7 @@ def run_pairs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, to
     lib = _lib.load_library()
     dev = block_table.device
     stream = torch.cuda.current_stream(dev).cuda_stream
-    ws = workspace or _lib.default_workspace(dev)
+    ws = workspace or _lib.default_workspace(dev, stream)
     ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
     a = _args(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, None, None, 0)
     with torch.cuda.device(dev):
@@ -199,13 +199,15 @@ def write_index_k(k_new: torch.Tensor, slot_ids: torch.Tensor, k_index_cache_fp8
 _attn_ws: dict = {}
 
 
-def _attn_workspace(dev: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-device workspace of the sparse attention (status header zeroed
-    once at allocation; grown when a call needs more)."""
-    ws = _attn_ws.get(dev)
+def _attn_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Workspace of the sparse attention per (device, stream), so calls on
+    different streams never share one (status header zeroed once at
+    allocation; grown when a call needs more)."""
+    key = (dev.index, int(stream))
+    ws = _attn_ws.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
-        _attn_ws[dev] = ws
+        _attn_ws[key] = ws
     return ws
 
 
@@ -241,7 +243,8 @@ def sparse_attention(q_nope: torch.Tensor, q_pe: torch.Tensor, ckv_cache: torch.
     lib = _lib.load_library()
     dev = q_nope.device
     with torch.cuda.device(dev):
-        ws = _attn_workspace(dev, int(lib.dsai_sparse_attn_workspace_size(T)))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        ws = _attn_workspace(dev, stream, int(lib.dsai_sparse_attn_workspace_size(T)))
         a = _lib.DsaiAttnArgs()
         a.q_nope, a.q_pe = q_nope.data_ptr(), q_pe.data_ptr()
         a.ckv_cache, a.kpe_cache = ckv_cache.data_ptr(), kpe_cache.data_ptr()
@@ -249,15 +252,16 @@ def sparse_attention(q_nope: torch.Tensor, q_pe: torch.Tensor, ckv_cache: torch.
         a.output, a.lse = output.data_ptr(), lse.data_ptr()
         a.sm_scale = float(sm_scale)
         a.num_tokens, a.num_pages = T, num_pages
-        _lib.check(lib.dsai_sparse_attn(ctypes.byref(a), ws.data_ptr(), ws.numel(),
-                                        torch.cuda.current_stream(dev).cuda_stream))
+        _lib.check(lib.dsai_sparse_attn(ctypes.byref(a), ws.data_ptr(), ws.numel(), stream))
 
 
 def read_attn_status(device=None) -> int:
     """Returns and clears the status bits of the sparse attention's workspace
-    on `device` (synchronises its current stream)."""
+    of `device` and its current stream (synchronises that stream)."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = _attn_ws.get(dev)
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    ws = _attn_ws.get((dev.index, torch.cuda.current_stream(dev).cuda_stream))
     if ws is None:
         return 0
     lib = _lib.load_library()
@@ -269,10 +273,12 @@ def read_attn_status(device=None) -> int:
 
 def read_status(device=None) -> int:
     """Returns and clears the device status bits of the default workspace of
-    `device` (synchronises its current stream)."""
+    `device` and its current stream, the one ``kernel()`` used when called
+    on that stream (synchronises the stream)."""
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    ws = _lib.default_workspace(dev)
-    return ws.read_status(torch.cuda.current_stream(dev).cuda_stream)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    ws = _lib.default_workspace(dev, stream)
+    return ws.read_status(stream)
 
 
 class IndexerGraph:

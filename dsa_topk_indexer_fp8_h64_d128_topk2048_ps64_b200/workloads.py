@@ -85,6 +85,25 @@ class Inputs:
         per_row = np.where(np.repeat(g_scored, R), 8192 + 256, 0) + 4 + 4 * TOPK
         return int(shared.sum() + per_row.sum())
 
+    def subset(self, rows, device="cpu") -> "Inputs":
+        """The batch restricted to `rows`, with only the pages those rows
+        reach, copied into a compact pool (block-table entries remapped,
+        entries past a row's last page set to 0).  Gives a small host copy
+        of a few rows of a batch whose full pool is too large to copy."""
+        rows = [int(r) for r in rows]
+        sl = self.seq_lens.cpu()[rows].to(torch.int64).clamp(0, self.max_pages * PAGE_SIZE)
+        bt = self.block_table.cpu()[rows].to(torch.int64)
+        npg = ((sl + PAGE_SIZE - 1) // PAGE_SIZE).tolist()
+        used = torch.unique(torch.cat([bt[i, :n] for i, n in enumerate(npg)] + [torch.zeros(1, dtype=torch.int64)]))
+        remap = {int(p): i for i, p in enumerate(used.tolist())}
+        bt_new = torch.zeros_like(bt)
+        for i, n in enumerate(npg):
+            bt_new[i, :n] = torch.tensor([remap[int(p)] for p in bt[i, :n].tolist()], dtype=torch.int64)
+        k_new = self.k_cache[used.to(self.k_cache.device)].to(device)
+        return Inputs(self.q[rows].to(device), k_new, self.weights[rows].to(device),
+                      sl.to(torch.int32).to(device), bt_new.to(torch.int32).to(device),
+                      name=f"{self.name}[{len(rows)} rows]", seed=self.seed, rows_per_seq=1)
+
     def scored_tokens(self) -> int:
         sl = self.seq_lens.cpu().numpy().astype(np.int64)
         sl = np.clip(sl, 0, self.max_pages * PAGE_SIZE)

@@ -145,6 +145,12 @@ DSAI_API int dsai_merge_pairs(const float* scores, const int32_t* tokens, int32_
  * in the reference. */
 DSAI_API int dsai_run_noalloc(const dsai_args* args, void* stream);
 
+/* The status word of dsai_run_noalloc's built-in array on the current
+ * device, as dsai_read_status gives it for a workspace: copied to
+ * *status_out (host), then cleared; 0 before the first call on the device.
+ * Synchronises `stream`.  No counterpart in the reference. */
+DSAI_API int dsai_noalloc_read_status(void* stream, int32_t* status_out);
+
 /* Index-K cache writer: quantises n_tokens new keys k_new [n_tokens, 128]
  * (fp32 or bf16, row-major) to e4m3 with one fp32 scale per token
  * (scale = max(max_d |k|, 1e-12) / 448, values clamp(k / scale, +-448),

@@ -13,14 +13,20 @@ order, :855-859 ordered keys, :897-905 / :1079-1097 short rows,
   * ``logits_numpy`` below: a vectorised numpy restatement of the scoring,
     used to cross-check the C code.
 
-Parity pinning: the reference ships no test vectors, its own definition
-reference (a Python implementation in the contest dataset) is not available
-here, and its CUDA kernel cannot run here.  The scoring stage is pinned to
-golden logits of DeepGEMM's published reference for paged FP8 MQA logits
-(as shipped in vLLM 0.22; tests/golden/indexer_logits_golden.npz, agreement
-to fp32 rounding, tests/test_oracle_pinned.py).  The selection stage (exact
-top-K, ties, -1 padding, physical ids) is restated from the reference
-kernel and checked by known answers (tests/test_oracle.py).
+Parity pinning: the reference ships no test vectors and its own
+definition reference (a Python implementation in the contest dataset) is
+not available here.  Two pins instead:
+  * the whole operator is pinned to the output of the reference's own CUDA
+    kernel (its TVM-FFI variant, solution/cuda/kernel.cu, built unmodified
+    by baseline/Makefile and run on a B200): the ids it wrote for seeded
+    inputs are tests/golden/reference_kernel_golden.npz, and the oracle's
+    exact top-2048 agrees with them up to the fp16 tie band of the
+    reference's fp16 logits (tests/test_reference_golden.py);
+  * the scoring stage is pinned to golden logits of DeepGEMM's published
+    reference for paged FP8 MQA logits (as shipped in vLLM 0.22;
+    tests/golden/indexer_logits_golden.npz, agreement to fp32 rounding,
+    tests/test_oracle_pinned.py).
+The selection rules are also checked by known answers (tests/test_oracle.py).
 """
 from __future__ import annotations
 
@@ -255,6 +261,36 @@ def check_row(gpu_ids, ora_logits, bt_row, L, gpu_logits=None, rtol=1e-2):
         sel[toks] = True
         assert gl[sel].min() >= gl[~sel].max(), "GPU set is not a top-K of its own logits"
     return dict(diff=len(only_gpu), gap=float(gap))
+
+
+# The reference kernel rounds its logits to fp16 before selecting
+# (solution/cuda/kernel.cu:228-229, solution/python/kernel.cu:830): rounding
+# is monotone, so its set can differ from the exact one only among tokens
+# whose fp16 logits tie the 2048th, i.e. within one fp16 ulp (at most 2^-10
+# relative) of it.  1e-3 covers that with fp32 summation-order noise to spare.
+REFERENCE_FP16_RTOL = 1e-3
+
+
+def set_diff_in_band(ids_a, ids_b, ora_logits, bt_row, L, rtol=REFERENCE_FP16_RTOL):
+    """Two top-K outputs of one row: rows with L <= 2048 must be identical;
+    longer rows may differ only in tokens whose oracle logit lies within
+    rtol*|s_K| of the oracle's K-th largest logit s_K.  Returns the number
+    of ids of `ids_a` missing from `ids_b`."""
+    a = np.asarray(ids_a).astype(np.int64)
+    b = np.asarray(ids_b).astype(np.int64)
+    if L <= TOPK:
+        assert np.array_equal(a, b), "short row differs"
+        return 0
+    phys = physical_ids(bt_row, L)
+    tok_of = {int(p): t for t, p in enumerate(phys)}
+    sa = {tok_of[int(p)] for p in a}
+    sb = {tok_of[int(p)] for p in b}
+    lg = np.asarray(ora_logits[:L], dtype=np.float64)
+    sK = np.sort(lg)[::-1][TOPK - 1]
+    band = rtol * abs(sK)
+    for t in sa ^ sb:
+        assert abs(lg[t] - sK) <= band + 1e-30, f"token {t}: logit {lg[t]} outside band {sK} +- {band}"
+    return len(sa - sb)
 
 
 def check_logits(gpu_logits, ora_logits, mag, seq_lens, rtol=1e-2, mag_tol=1e-4):

@@ -174,3 +174,8 @@ def test_noalloc_rejects_without_device(dsai_lib):
     a = _args(rows=256, max_pages=2048, num_pages=1)  # far more than its 16 MiB array
     assert dsai_lib.dsai_run_noalloc(ctypes.byref(a), None) == -2
     assert b"static scratch" in dsai_lib.dsai_last_error()
+    for bad in (dict(rows=-1, max_pages=4, num_pages=1), dict(rows=2, max_pages=-4, num_pages=1),
+                dict(rows=2, max_pages=4, num_pages=-1)):
+        assert dsai_lib.dsai_run_noalloc(ctypes.byref(_args(**bad)), None) == -1
+        assert b"negative size" in dsai_lib.dsai_last_error()
+    assert dsai_lib.dsai_noalloc_read_status(None, None) == -1

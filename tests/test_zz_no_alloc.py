@@ -9,9 +9,12 @@ Checked here through the C ABI: two calls in a row give the same top-2048 as
 the ordinary entry point dsai_run (which gets its own workspace) — short rows
 bit-exact, long rows the same set up to tokens whose logit ties the 2048th
 largest (the tolerance the parity tests use; both paths compute identical
-logits).  The array keeps the previous call's contents, so the second call
-also checks that a call leaves it clean, and a third call with more rows
-checks the newly used part of it.  This file is collected last on purpose.
+logits) — and the same answer as the CPU oracle under the parity rules of the
+other GPU tests.  The array keeps the previous call's contents, so the second
+call also checks that a call leaves it clean, and a third call with more rows
+checks the newly used part of it.  After the calls the array's status word
+(read through dsai_noalloc_read_status) must be clear.  This file is
+collected last on purpose.
 """
 import ctypes
 
@@ -71,10 +74,26 @@ def _same_topk(got, exp, logits, g):
                 assert row[token_of[pid]] == kth, f"row {b}: id {pid} differs outside the tie band"
 
 
-def test_noalloc_matches_run_on_two_calls_in_a_row():
+def _noalloc_status(lib, stream):
+    v = ctypes.c_int32(-1)
+    assert lib.dsai_noalloc_read_status(stream, ctypes.byref(v)) == 0, lib.dsai_last_error()
+    return int(v.value)
+
+
+def _oracle_check(oracle_mod, inp, ids):
+    """The no-alloc ids against the CPU oracle (parity rules of the GPU tests)."""
+    d = inp.numpy()
+    lg = oracle_mod.logits(d["q"], d["k_cache"], d["weights"], d["seq_lens"], d["block_table"],
+                           num_pages=d["num_pages"], nthreads=8)
+    for b in range(inp.rows):
+        oracle_mod.check_row(ids[b], lg[b], d["block_table"][b], int(d["seq_lens"][b]))
+
+
+def test_noalloc_matches_run_on_two_calls_in_a_row(oracle_mod):
     lib = _lib.load_library()
     stream = torch.cuda.current_stream(DEV).cuda_stream
-    small = W.make_inputs([1500, 4096, 9001, 2049, 64, 20000], seed=41).to(DEV)
+    small_cpu = W.make_inputs([1500, 4096, 9001, 2049, 64, 20000], seed=41)
+    small = small_cpu.to(DEV)
     exp, lg = _expected(lib, small, stream)
     for _ in range(2):
         out = small.out()
@@ -82,14 +101,19 @@ def test_noalloc_matches_run_on_two_calls_in_a_row():
         assert rc == 0, lib.dsai_last_error()
         torch.cuda.synchronize()
         _same_topk(out.cpu().numpy(), exp, lg, small)
+    _oracle_check(oracle_mod, small_cpu, out.cpu().numpy())
+    assert _noalloc_status(lib, stream) == 0
     # more rows than before: part of the array that held logits now holds histograms
-    big = W.config_inputs(1, rows=16, seed=42).to(DEV)
+    big_cpu = W.config_inputs(1, rows=16, seed=42)
+    big = big_cpu.to(DEV)
     exp2, lg2 = _expected(lib, big, stream)
     out = big.out()
     rc = lib.dsai_run_noalloc(ctypes.byref(_args(big, out)), stream)
     assert rc == 0, lib.dsai_last_error()
     torch.cuda.synchronize()
     _same_topk(out.cpu().numpy(), exp2, lg2, big)
+    _oracle_check(oracle_mod, big_cpu, out.cpu().numpy())
+    assert _noalloc_status(lib, stream) == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_array():

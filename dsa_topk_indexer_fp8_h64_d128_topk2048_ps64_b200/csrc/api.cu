@@ -237,6 +237,15 @@ int check_scoring_args(const dsai_args* a) {
   return DSAI_OK;
 }
 
+// The fused launch (fused.cu) serves batches of many independent rows that
+// fit one launch: at least one row per four SMs (fewer rows are selected
+// faster by several CTAs per row, select_split_kernel), rows scored one by
+// one (rows_per_seq <= 1).
+bool use_fused(const dsai_args* a, int sms) {
+  return dsai::fused_enabled() && a->rows <= dsai::kMaxRowsPerLaunch && a->rows_per_seq <= 1 &&
+         static_cast<long long>(a->rows) * 4 >= sms;
+}
+
 // Scores all needed rows into `logits`, chunking by the per-launch row limit.
 int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, bool score_all, int sms,
                 cudaStream_t stream) {
@@ -323,6 +332,39 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   uint32_t* hist = ws_hist(workspace);
   rc = prepare_hist(workspace, a->rows, stream);
   if (rc) return rc;
+  if (use_fused(a, dev.sms)) {
+    // Many independent rows: scoring and selection in one launch, each row
+    // selected as soon as its scoring completes.
+    CUtensorMap tq, tk, ts;
+    rc = get_map(kMapQ, a->q, static_cast<uint64_t>(a->rows) * dsai::kHeads, &tq);
+    if (rc) return rc;
+    rc = get_map(kMapK, a->k_cache, static_cast<uint64_t>(a->num_pages), &tk);
+    if (rc) return rc;
+    rc = get_map(kMapS, a->k_cache, static_cast<uint64_t>(a->num_pages), &ts);
+    if (rc) return rc;
+    dsai::FusedLaunch fp;
+    fp.weights = a->weights;
+    fp.seq_lens = a->seq_lens;
+    fp.block_table = a->block_table;
+    fp.logits = logits;
+    fp.hist = hist;
+    fp.cand = ws_cand(workspace, a->rows);
+    fp.ws = status;
+    fp.out_ids = a->topk_indices;
+    fp.rows = a->rows;
+    fp.max_pages = a->max_pages;
+    fp.num_pages = a->num_pages;
+    fp.ld = a->max_pages * dsai::kPage;
+    fp.score_all = score_all ? 1 : 0;
+    fp.sms = dev.sms;
+    cudaError_t e = dsai::launch_fused(fp, tq, tk, ts, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "fused kernel launch");
+    if (a->ev_after_score) {  // no boundary inside the fused launch: recorded after it
+      e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    }
+    return DSAI_OK;
+  }
   rc = run_scoring(a, logits, hist, status, score_all, dev.sms, stream);
   if (rc) return rc;
   if (a->ev_after_score) {

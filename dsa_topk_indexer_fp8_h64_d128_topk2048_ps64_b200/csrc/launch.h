@@ -36,6 +36,32 @@ cudaError_t launch_score(const ScoreLaunch& p, const CUtensorMap& tmap_q, const 
 cudaError_t launch_score_groups(const ScoreLaunch& p, int rows_per_group, const CUtensorMap& tmap_q,
                                 const CUtensorMap& tmap_k, const CUtensorMap& tmap_s, cudaStream_t stream);
 
+struct FusedLaunch {
+  const float* weights;
+  const int32_t* seq_lens;
+  const int32_t* block_table;
+  float* logits;      // [rows, ld]
+  uint32_t* hist;     // [rows, kHistStride] (zero on entry, left zero)
+  uint32_t* cand;     // [rows, 2, kSplitCap] pivot-bin lists
+  int* ws;            // workspace header (status word and the queue's control words)
+  int32_t* out_ids;   // [rows, 2048]
+  int rows;           // at most kMaxRowsPerLaunch
+  int max_pages;
+  int num_pages;
+  int ld;
+  int score_all;
+  int sms;
+};
+
+// Scoring and top-2048 selection of many rows in one persistent launch
+// (fused.cu): scorer CTAs over an interleaved tile schedule, selector CTAs
+// that select each row as soon as its scoring completes.  Opt-in:
+// fused_enabled() is true only with DSAI_FUSED=1 in the environment (it is
+// slower than the two-launch path on the benchmark shapes).
+bool fused_enabled();
+cudaError_t launch_fused(const FusedLaunch& p, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
+                         const CUtensorMap& tmap_s, cudaStream_t stream);
+
 struct AttnLaunch {
   const void* q_nope;
   const void* q_pe;

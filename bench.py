@@ -504,14 +504,15 @@ def strong_config2(args, world, rank, local) -> dict:
         allc = [torch.zeros_like(cnt) for _ in range(world)]
         dist.all_gather(allc, cnt)
         counts = [int(c.item()) for c in allc]
+        gbuf = torch.empty((world, max(counts), 2048), dtype=torch.int32, device=dev)
         for _ in range(3):
-            D.gather_rows(out, counts)
+            D.gather_rows(out, counts, buf=gbuf)
         torch.cuda.synchronize()
         dist.barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
         for _ in range(10):
-            D.gather_rows(out, counts)
+            D.gather_rows(out, counts, buf=gbuf)
         g1.record()
         torch.cuda.synchronize()
         tg = torch.tensor([g0.elapsed_time(g1) / 10], device=dev)

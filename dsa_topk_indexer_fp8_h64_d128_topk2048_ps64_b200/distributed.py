@@ -108,14 +108,26 @@ def row_sharded_kernel(q, k_cache, weights, seq_lens, block_table, topk_indices)
     solution.kernel(q, k_cache, weights, seq_lens, block_table, topk_indices)
 
 
-def gather_rows(local_out: torch.Tensor, counts: list[int], group=None) -> torch.Tensor:
+def gather_rows(local_out: torch.Tensor, counts: list[int], group=None, buf: torch.Tensor | None = None) -> torch.Tensor:
     """All-gathers every rank's [rows_g, 2048] output into one [sum, 2048]
-    tensor on every rank (rows_g given by `counts`)."""
+    tensor on every rank (rows_g given by `counts`).  One collective into a
+    [world, max(counts), 2048] buffer (pass `buf` to reuse one across calls);
+    the result is a view when every rank has the same row count."""
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return local_out
-    m = max(counts)
-    pad = torch.full((m, TOPK), -1, dtype=local_out.dtype, device=local_out.device)
-    pad[: local_out.shape[0]] = local_out
-    bufs = [torch.empty_like(pad) for _ in counts]
-    dist.all_gather(bufs, pad, group=group)
-    return torch.cat([b[:n] for b, n in zip(bufs, counts)])
+    world, m = len(counts), max(counts)
+    if buf is None or tuple(buf.shape) != (world, m, TOPK) or buf.dtype != local_out.dtype:
+        buf = torch.empty((world, m, TOPK), dtype=local_out.dtype, device=local_out.device)
+    n = local_out.shape[0]
+    if n == m:
+        send = local_out.contiguous()
+    else:
+        send = torch.full((m, TOPK), -1, dtype=local_out.dtype, device=local_out.device)
+        send[:n] = local_out
+    if hasattr(dist, "all_gather_into_tensor") and dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(buf.view(world * m, TOPK), send, group=group)
+    else:
+        dist.all_gather(list(buf.unbind(0)), send, group=group)
+    if all(c == m for c in counts):
+        return buf.view(world * m, TOPK)
+    return torch.cat([buf[g, :c] for g, c in enumerate(counts)])

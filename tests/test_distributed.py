@@ -105,3 +105,41 @@ def test_split_row_on_two_gloo_ranks_matches_direct(oracle_mod, seq_len):
             assert set(results[r].tolist()) == set(direct[0].tolist())
     planted = oracle_mod.physical_ids(d["block_table"][0], seq_len)[[3, seq_len // 2 - 1, seq_len // 2, seq_len - 1]]
     assert set(planted.tolist()) <= set(results[0].tolist())
+
+
+def _gather_worker(rank, world, port, result_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        counts = [3, 2]
+        local = torch.arange(counts[rank] * TOPK, dtype=torch.int32).view(counts[rank], TOPK) + 100000 * rank
+        buf = torch.empty((world, max(counts), TOPK), dtype=torch.int32)
+        got = D.gather_rows(local, counts, buf=buf)
+        got2 = D.gather_rows(local, counts)  # without a caller buffer
+        result_q.put((rank, got.numpy().copy(), got2.numpy().copy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_rows_on_two_gloo_ranks():
+    """Rows sharded unevenly (3 and 2 rows): every rank gets all 5 rows in
+    rank order."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, a, b = q.get(timeout=120)
+        results[r] = (a, b)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    exp = np.concatenate([np.arange(3 * TOPK, dtype=np.int32).reshape(3, TOPK),
+                          np.arange(2 * TOPK, dtype=np.int32).reshape(2, TOPK) + 100000])
+    for r in range(world):
+        assert np.array_equal(results[r][0], exp) and np.array_equal(results[r][1], exp)

@@ -445,7 +445,7 @@ def kernel_times(sets, outs, R, n_ev):
     return score_ms, select_ms
 
 
-def extra_config(config: int, steps: int, warmup: int, dev) -> dict:
+def extra_config(config: int, steps: int, warmup: int, dev, with_reference: bool = True) -> dict:
     """One more benchmark config on this GPU (N = 1): µs per call over K
     back-to-back calls (rotating copies when the pool is smaller than four
     times L2), algorithmic GB/s and fraction of the measured HBM peak, the
@@ -473,9 +473,63 @@ def extra_config(config: int, steps: int, warmup: int, dev) -> dict:
     if R > 1:
         tpeak, _ = measured_fp8_peak()
         out["score_frac_of_fp8_peak"] = round(score_flops(base) / (score_ms / 1e3) / 1e12 / tpeak, 4)
+    if with_reference:
+        # the reference scores every row on its own (it has no shared-page groups)
+        ref = time_reference_kernel(sets, max(3, min(steps, 20)), 3)
+        if "us_per_call" in ref:
+            ref["value"] = round(alg / (ref["us_per_call"] / 1e6) / 1e9, 1)
+            ref["note"] = "value: this config's algorithmic bytes per call over the reference's time"
+        out["reference_kernel"] = ref
     del sets, outs, base
     torch.cuda.empty_cache()
     return out
+
+
+def small_shape_latency(steps: int, warmup: int, dev) -> dict:
+    """Latency of small calls (the contest's workload sizes: B <= 31 rows of
+    at most 91 pages), where per-call host work and kernel latency dominate:
+    the drop-in kernel(...) called back to back (CUDA events over the calls,
+    and the host time to issue one call), and the same call replayed from a
+    CUDA graph (IndexerGraph; device time only)."""
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import IndexerGraph
+    shapes = {"config0 (B=2, L {1500, 4096}, 64 pages)": W.config_inputs(0, device=dev),
+              "B=14, L 1924..5824, 91 pages": W.make_inputs(list(range(5824 - 13 * 300, 5825, 300)), max_pages=91,
+                                                           seed=5, device=dev)}
+    res = {}
+    for name, g in shapes.items():
+        out = g.out()
+
+        def call():
+            kernel(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out)
+
+        for _ in range(warmup + 20):
+            call()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            call()
+        t1 = time.perf_counter()
+        e1.record()
+        torch.cuda.synchronize()
+        eager = e0.elapsed_time(e1) / steps * 1e3
+        host = (t1 - t0) / steps * 1e6
+        gr = IndexerGraph(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out)
+        for _ in range(warmup + 20):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(steps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name] = {"eager_us_per_call": round(eager, 2), "host_us_per_call": round(host, 2),
+                     "graph_replay_us_per_call": round(e0.elapsed_time(e1) / steps * 1e3, 2)}
+        del gr
+    res["timing"] = (f"{steps} back-to-back calls, CUDA events; host = time to issue one kernel(...) call "
+                     "(perf_counter, no synchronisation inside)")
+    return res
 
 
 def strong_config2(args, world, rank, local) -> dict:
@@ -599,9 +653,14 @@ def split_config3(args, world, rank, local, steps: int | None = None) -> dict:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item()) / steps
     alg = g.algorithmic_bytes()
+    ref = None
+    if world == 1 and not args.no_reference_kernel:
+        rsets = [W.Inputs(g.q, pool, g.weights, g.seq_lens, g.block_table) for pool in pools]
+        ref = time_reference_kernel(rsets, max(3, min(steps, 200)), 3)
     del pools
     torch.cuda.empty_cache()
-    return {"workload": f"config3: {W.CONFIGS[3]}", "scaling": "strong", "seq_len": L,
+    extra = {"reference_kernel": ref} if ref is not None else {}
+    return {**extra, "workload": f"config3: {W.CONFIGS[3]}", "scaling": "strong", "seq_len": L,
             "pages_per_rank": p1 - p0, "seed": seed, "us_per_call": round(ms * 1e3, 2),
             "value": round(alg / (ms / 1e3) / 1e9, 1), "unit": "GB/s", "steps": steps,
             "l2": "16 rotating copies of the 9.5 MB page pool (152 MB > 126 MB L2)",
@@ -740,9 +799,12 @@ def bench_ours(args, world, rank, local):
         strong = strong_config2(args, world, rank, local)
         split = split_config3(args, world, rank, local, steps=max(3, min(args.steps, 500)))
     extras = {}
+    small = None
     if world == 1 and args.config == 1 and not args.no_extras:
+        small = small_shape_latency(max(10, min(args.steps, 2000)), args.warmup, dev)
         for c in (2, 4):
-            extras[f"config{c}"] = extra_config(c, max(3, min(args.steps, args.extra_steps)), args.warmup, dev)
+            extras[f"config{c}"] = extra_config(c, max(3, min(args.steps, args.extra_steps)), args.warmup, dev,
+                                                with_reference=not args.no_reference_kernel)
 
     if rank != 0:
         return None
@@ -798,6 +860,8 @@ def bench_ours(args, world, rank, local):
         line["split_config3"] = split
     if extras:
         line["configs"] = extras
+    if small is not None:
+        line["small_shapes"] = small
     if world == 1 and R == 1 and not args.no_reference_kernel:
         line["reference_kernel"] = time_reference_kernel(sets, max(3, min(args.steps, 200)), args.warmup)
     if world == 1 and not args.no_cpu_baseline:

@@ -87,6 +87,8 @@ _lib_lock = threading.Lock()
 def load_library(path: Path | None = None) -> ctypes.CDLL:
     """Loads libdsai.so once; raises if it is missing."""
     global _lib
+    if _lib is not None and path is None:
+        return _lib
     with _lib_lock:
         if _lib is not None:
             return _lib
@@ -147,8 +149,12 @@ class Workspace:
     def __init__(self, device: torch.device):
         self.device = torch.device(device)
         self.buf: torch.Tensor | None = None
+        self._shape = None      # (rows, max_pages) of the last get()
+        self._span = (0, 0)     # (pointer, bytes) it returned
 
     def get(self, rows: int, max_pages: int, stream: int) -> tuple[int, int]:
+        if self._shape == (rows, max_pages) and self.buf is not None:
+            return self._span
         need = workspace_size(rows, max_pages)
         if self.buf is None or self.buf.numel() < need:
             size = max(need, 1 << 20)
@@ -156,7 +162,9 @@ class Workspace:
                 size = max(size, 2 * self.buf.numel())
             self.buf = torch.empty(size, dtype=torch.uint8, device=self.device)
             check(load_library().dsai_workspace_init(self.buf.data_ptr(), self.buf.numel(), stream))
-        return self.buf.data_ptr(), self.buf.numel()
+        self._shape = (rows, max_pages)
+        self._span = (self.buf.data_ptr(), self.buf.numel())
+        return self._span
 
     def read_status(self, stream: int) -> int:
         """Returns and clears the device status bits (synchronises `stream`)."""

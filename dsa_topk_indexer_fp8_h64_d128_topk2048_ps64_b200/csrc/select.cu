@@ -457,6 +457,7 @@ constexpr int kWRound = kWThreads * kCPer;  // 32768 entries per round
 constexpr int kWCap = 8192;                 // pivot-bin keys kept
 constexpr int kWBtCache = 2048;             // block-table entries of a row in smem (131072 tokens)
 constexpr int kSmall = 64;                  // second-digit bin small enough for one warp to rank
+constexpr int kWideShortRow = 16384;        // rows this short get one wide CTA each, however few
 
 struct WideSmem {
   float4 vals[kCPer / 4][kWThreads];  // the current round's logits
@@ -1395,7 +1396,8 @@ SelectShape select_shape(int rows, int max_pages, int sms) {
   const bool wide = true;
 #else
   // One wide CTA per row once the rows alone occupy a good share of the SMs.
-  const bool wide = static_cast<long long>(rows) * 4 >= static_cast<long long>(sms);
+  const bool wide = static_cast<long long>(rows) * 4 >= static_cast<long long>(sms) ||
+                    static_cast<long long>(max_pages) * kPage <= kWideShortRow;
 #endif
   if (wide) {
     sh.threads = kWThreads;
@@ -1448,11 +1450,15 @@ cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
   cudaError_t e = ensure_attrs();
   if (e != cudaSuccess) return e;
   if (p.rows <= 0) return cudaSuccess;
-  if (p.cand && use_split_select() && static_cast<long long>(p.rows) * 4 < static_cast<long long>(p.sms)) {
-    // Few rows: several CTAs per row.  (With many rows the one-CTA-per-row
-    // kernel is faster: the split kernel's chain of dependent steps per CTA
-    // — histogram, slot atomic, ticket, refinement — is longer than the wide
-    // CTA's, measured 48.4 against 42.5 us per call at B = 64.)
+  if (p.cand && use_split_select() && static_cast<long long>(p.rows) * 4 < static_cast<long long>(p.sms) &&
+      static_cast<long long>(p.max_pages) * kPage > kWideShortRow) {
+    // Few long rows: several CTAs per row.  (With many rows the
+    // one-CTA-per-row kernel is faster: the split kernel's chain of dependent
+    // steps per CTA — histogram, slot atomic, ticket, refinement — is longer
+    // than the wide CTA's, measured 48.4 against 42.5 us per call at B = 64;
+    // so it is for few short rows, whose logits one SM reads quickly: 14.2
+    // against 16.4 us per call on config 0, 14.5 against 18.4 us at 14 rows of
+    // up to 91 pages, CUDA-graph replays.)
     const long long max_len = static_cast<long long>(p.max_pages) * kPage;
     long long cpr = (max_len + kSChunk - 1) / kSChunk;
     if (cpr < 1) cpr = 1;

@@ -23,6 +23,18 @@ __all__ = ["kernel", "run", "run_pairs", "merge_pairs", "read_status", "write_in
            "sparse_attention", "read_attn_status"]
 
 _FP8 = getattr(torch, "float8_e4m3fn", None)
+# Per-call host work is most of the cost of a small call: the current device
+# and the raw stream handle are read without building torch.cuda objects.
+_current_device = torch._C._cuda_getDevice
+_current_raw_stream = torch._C._cuda_getCurrentRawStream
+
+
+def _call_on(dev_index: int, fn, *args) -> int:
+    """Calls fn(*args) with `dev_index` as the current CUDA device."""
+    if _current_device() == dev_index:
+        return fn(*args)
+    with torch.cuda.device(dev_index):
+        return fn(*args)
 
 
 def _req(cond: bool, msg: str) -> None:
@@ -100,7 +112,8 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
              and logits_out.numel() == rows * max_pages * _lib.PAGE_SIZE,
              "logits_out must be float32 contiguous CUDA [B, max_pages*64]")
     dev = block_table.device
-    stream = torch.cuda.current_stream(dev).cuda_stream
+    idx = dev.index
+    stream = _current_raw_stream(idx)
     ws = workspace or _lib.default_workspace(dev, stream)
     ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
     a = _args(q_index_fp8 if needs_scoring else None, k_index_cache_fp8 if needs_scoring else None,
@@ -110,8 +123,7 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
         a.num_pages = k_index_cache_fp8.numel() // _lib.PAGE_BYTES
     if event_after_score is not None:
         a.ev_after_score = event_after_score.cuda_event
-    with torch.cuda.device(dev):
-        _lib.check(lib.dsai_run(ctypes.byref(a), ws_ptr, ws_bytes, stream))
+    _lib.check(_call_on(idx, lib.dsai_run, ctypes.byref(a), ws_ptr, ws_bytes, stream))
 
 
 def kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices):

@@ -67,25 +67,33 @@ METRIC = "index-K HBM GB/s per indexer call (score + top-2048), B=64 decode"
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one scoring launch from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of this bench's workload,
-# with the SHA-256 of the kernel sources that capture ran.  roofline.traffic
+# with the SHA-256 of that kernel's device sources (KERNEL_SOURCES) when it
+# was captured.  roofline.traffic
 # reports it only while the sources still hash the same; otherwise it is
 # null and the old capture is shown as traffic_last_profiled.
 SCORE_TRAFFIC = {
-    1: {"bytes": 156_324_096 + 4_711_168, "src_sha256": "", "kernel": "score_kernel"},
-    4: {"bytes": 156_743_680 + 6_461_696, "src_sha256": "", "kernel": "score_mq_kernel<4>"},
+    1: {"bytes": 156_326_656 + 5_183_488, "kernel": "score_kernel",
+        "src_sha256": "d68907fb8cba24ffb545aa4cadda61aab1e7aa97c8ba6973a1b7d2ea6fe5f7e2"},
+    4: {"bytes": 156_798_464 + 8_856_832, "kernel": "score_mq_kernel<4>",
+        "src_sha256": "485f0dec96c7cbd5e1e23e69eeb41448adb0126de3960579c144803ccb97a419"},
 }
 N_SETS = 3
 
 
-def kernel_sources_sha256() -> str:
-    """SHA-256 over the CUDA sources and headers the library is built from."""
+KERNEL_SOURCES = {
+    "score_kernel": ["score.cu", "common.cuh", "sm100.cuh", "tiles.cuh"],
+    "score_mq_kernel<4>": ["score_mq.cu", "common.cuh", "sm100.cuh", "tiles.cuh"],
+}
+
+
+def kernel_sources_sha256(kernel: str) -> str:
+    """SHA-256 over the device sources one kernel is compiled from."""
     import hashlib
     h = hashlib.sha256()
     csrc = REPO / "dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200" / "csrc"
-    for f in sorted(list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh")) + list(csrc.glob("*.h"))):
-        h.update(f.name.encode())
-        h.update(f.read_bytes())
-    h.update((REPO / "include" / "dsai.h").read_bytes())
+    for name in KERNEL_SOURCES[kernel]:
+        h.update(name.encode())
+        h.update((csrc / name).read_bytes())
     return h.hexdigest()
 
 
@@ -93,7 +101,7 @@ def traffic_entry(config: int, rows_per_seq: int, config_rps: int) -> dict:
     cap = SCORE_TRAFFIC.get(config)
     if cap is None or rows_per_seq != config_rps:
         return {"traffic": None, "traffic_source": "no ncu capture for this workload"}
-    if cap["src_sha256"] and cap["src_sha256"] == kernel_sources_sha256():
+    if cap["src_sha256"] and cap["src_sha256"] == kernel_sources_sha256(cap["kernel"]):
         return {"traffic": cap["bytes"],
                 "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of this build"}
     return {"traffic": None, "traffic_last_profiled": cap["bytes"],

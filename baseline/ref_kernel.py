@@ -18,8 +18,12 @@ from pathlib import Path
 
 LIB = Path(__file__).resolve().parent / "_ref" / "libref_tvm_indexer.so"
 SOURCE = "solution/cuda/kernel.cu (TVM-FFI variant, unmodified)"
+ACTIVE_NAME = "dsa_topk_indexer_ref_active"
+ACTIVE_SOURCE = ("solution/python/kernel.cu (the active path; static K ring moved to dynamic shared "
+                 "memory to build with nvcc 12.9, baseline/build_active_variant.py)")
 
 _fn = None
+_active = None
 
 
 def available() -> tuple[bool, str]:
@@ -50,3 +54,33 @@ def load():
 def kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices) -> None:
     """Calls the reference kernel on torch's current stream."""
     load()(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)
+
+
+def active_lib() -> Path | None:
+    hits = sorted((Path(__file__).resolve().parent / "_ref").glob(ACTIVE_NAME + "*.so"))
+    return hits[0] if hits else None
+
+
+def active_available() -> tuple[bool, str]:
+    if active_lib() is None:
+        return False, "active variant not built (python baseline/build_active_variant.py needs the reference checkout)"
+    return True, ""
+
+
+def active_kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices) -> None:
+    """The reference's active path: its torch extension's `run`, which
+    solution/python/solution.py::kernel forwards to (solution.py:25-26)."""
+    global _active
+    if _active is None:
+        import importlib.machinery
+        import importlib.util
+        import torch  # noqa: F401  (the extension links against torch)
+        so = active_lib()
+        if so is None:
+            raise RuntimeError(active_available()[1])
+        loader = importlib.machinery.ExtensionFileLoader(ACTIVE_NAME, str(so))
+        spec = importlib.util.spec_from_file_location(ACTIVE_NAME, str(so), loader=loader)
+        mod = importlib.util.module_from_spec(spec)
+        loader.exec_module(mod)
+        _active = mod
+    _active.run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)

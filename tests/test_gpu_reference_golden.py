@@ -1,9 +1,10 @@
 """GPU parity of this indexer against the reference's own CUDA kernel.
 
 Our drop-in kernel(...) runs on the inputs of tests/golden/
-reference_kernel_golden.npz (the ids the reference's kernel,
-solution/cuda/kernel.cu, wrote for them on a B200) and must agree with the
-reference: rows with seq_len <= 2048 and the -1 padding bit for bit, longer
+reference_kernel_golden.npz and reference_kernel_active_golden.npz (the ids
+the reference's kernels wrote for them on a B200: the TVM-FFI variant
+solution/cuda/kernel.cu, and the active path solution/python/kernel.cu) and
+must agree with the reference: rows with seq_len <= 2048 and the -1 padding bit for bit, longer
 rows as sets except among tokens whose oracle logit ties the 2048th within
 the reference's fp16 rounding (oracle.REFERENCE_FP16_RTOL).  The differences
 are counted and printed.
@@ -20,14 +21,17 @@ from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import kernel, read_status
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 GOLDEN = Path(__file__).resolve().parent / "golden"
-NPZ = GOLDEN / "reference_kernel_golden.npz"
+NPZ = GOLDEN / "reference_kernel_golden.npz"                 # solution/cuda/kernel.cu
+NPZ_ACTIVE = GOLDEN / "reference_kernel_active_golden.npz"   # solution/python/kernel.cu
 
 
-@pytest.mark.skipif(not NPZ.exists(), reason="reference-kernel golden vectors not generated yet")
-def test_kernel_matches_reference_kernel_outputs(oracle_mod):
+@pytest.mark.parametrize("npz", [NPZ, NPZ_ACTIVE], ids=["tvm_ffi_variant", "active_variant"])
+def test_kernel_matches_reference_kernel_outputs(oracle_mod, npz):
+    if not npz.exists():
+        pytest.skip(f"{npz.name} not generated")
     sys.path.insert(0, str(GOLDEN))
     import make_reference_kernel_golden as G
-    z = np.load(NPZ)
+    z = np.load(npz)
     diffs, rows = 0, 0
     for name, inp in G.cases().items():
         assert G.digest(inp) == str(z[f"{name}_sha256"])
@@ -48,4 +52,4 @@ def test_kernel_matches_reference_kernel_outputs(oracle_mod):
         for b, toks in inp.planted.items():  # config 3: every planted token selected by both
             phys = {int(inp.block_table[b, t // 64]) * 64 + t % 64 for t in toks}
             assert phys <= set(ours[b].tolist()) and phys <= set(ref[b].tolist())
-    print(f"ours vs reference kernel: {rows} rows, {diffs} ids differ inside the fp16 tie band")
+    print(f"ours vs {npz.name}: {rows} rows, {diffs} ids differ inside the fp16 tie band")

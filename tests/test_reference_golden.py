@@ -19,6 +19,9 @@ import pytest
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 NPZ = GOLDEN / "reference_kernel_golden.npz"
+# The same cases through the reference's active path (solution/python/kernel.cu,
+# baseline/build_active_variant.py), when its outputs have been generated.
+NPZ_ACTIVE = GOLDEN / "reference_kernel_active_golden.npz"
 
 
 def _cases():
@@ -27,10 +30,12 @@ def _cases():
     return G
 
 
-@pytest.mark.skipif(not NPZ.exists(), reason="reference-kernel golden vectors not generated yet")
-def test_oracle_matches_reference_kernel_outputs(oracle_mod):
+@pytest.mark.parametrize("npz", [NPZ, NPZ_ACTIVE], ids=["tvm_ffi_variant", "active_variant"])
+def test_oracle_matches_reference_kernel_outputs(oracle_mod, npz):
+    if not npz.exists():
+        pytest.skip(f"{npz.name} not generated")
     G = _cases()
-    z = np.load(NPZ)
+    z = np.load(npz)
     total_diff = 0
     rows_checked = 0
     for name, inp in G.cases().items():
@@ -51,4 +56,4 @@ def test_oracle_matches_reference_kernel_outputs(oracle_mod):
             for b in range(inp.rows):
                 if int(d["seq_lens"][b]) > 2048:
                     assert len(set(ref_ids[b].tolist()) & set(exact[b].tolist())) >= 2048 - 64, f"{name} row {b}"
-    print(f"reference kernel vs oracle: {rows_checked} rows, {total_diff} ids differ inside the fp16 tie band")
+    print(f"{npz.name} vs oracle: {rows_checked} rows, {total_diff} ids differ inside the fp16 tie band")

@@ -173,6 +173,20 @@ int prepare_hist(void* ws, int32_t rows, cudaStream_t stream) {
   return DSAI_OK;
 }
 
+// Workspaces whose logits region holds the fused launch's sentinel, with the
+// geometry (rows, row stride) it was filled for.  The fused launch leaves the
+// region so; any other launch that writes logits into it clears the entry.
+struct SentinelGeom {
+  int32_t rows;
+  int32_t ld;
+};
+std::unordered_map<const void*, SentinelGeom> g_ws_sentinel;
+
+void forget_sentinel(const void* ws) {
+  std::lock_guard<std::mutex> g(g_ws_mu);
+  g_ws_sentinel.erase(ws);
+}
+
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // Workspace layout: [header 256 B | per-row histogram blocks (4096 bins and
@@ -242,8 +256,9 @@ int check_scoring_args(const dsai_args* a) {
 // faster by several CTAs per row, select_split_kernel), rows scored one by
 // one (rows_per_seq <= 1).
 bool use_fused(const dsai_args* a, int sms) {
+  const bool score_all = (a->flags & DSAI_FLAG_SCORE_ALL_ROWS) != 0;
   return dsai::fused_enabled() && a->rows <= dsai::kMaxRowsPerLaunch && a->rows_per_seq <= 1 &&
-         static_cast<long long>(a->rows) * 4 >= sms;
+         static_cast<long long>(a->rows) * 4 >= sms && (!score_all || a->logits_out != nullptr);
 }
 
 // Scores all needed rows into `logits`, chunking by the per-launch row limit.
@@ -301,6 +316,7 @@ int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(workspace)");
   std::lock_guard<std::mutex> g(g_ws_mu);
   g_ws_clean_rows[workspace] = INT_MAX;
+  g_ws_sentinel.erase(workspace);
   return DSAI_OK;
 }
 
@@ -342,13 +358,27 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
     if (rc) return rc;
     rc = get_map(kMapS, a->k_cache, static_cast<uint64_t>(a->num_pages), &ts);
     if (rc) return rc;
+    const int32_t ld = a->max_pages * dsai::kPage;
+    const size_t lbytes = static_cast<size_t>(a->rows) * static_cast<size_t>(ld) * sizeof(float);
+    const unsigned char sent = static_cast<unsigned char>(dsai::fused_logits_sentinel() & 0xFFu);
+    bool fill = a->logits_out != nullptr;  // the caller's buffer: filled every call
+    if (!fill) {
+      std::lock_guard<std::mutex> g(g_ws_mu);
+      auto it = g_ws_sentinel.find(workspace);
+      fill = it == g_ws_sentinel.end() || it->second.rows != a->rows || it->second.ld != ld;
+      g_ws_sentinel[workspace] = SentinelGeom{a->rows, ld};
+    }
+    if (fill) {
+      cudaError_t e = cudaMemsetAsync(logits, sent, lbytes, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(logits sentinel)");
+    }
     dsai::FusedLaunch fp;
     fp.weights = a->weights;
     fp.seq_lens = a->seq_lens;
     fp.block_table = a->block_table;
     fp.logits = logits;
     fp.hist = hist;
-    fp.cand = ws_cand(workspace, a->rows);
+    fp.keep_logits = a->logits_out != nullptr ? 1 : 0;
     fp.ws = status;
     fp.out_ids = a->topk_indices;
     fp.rows = a->rows;
@@ -365,6 +395,7 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
     }
     return DSAI_OK;
   }
+  if (!a->logits_out) forget_sentinel(workspace);
   rc = run_scoring(a, logits, hist, status, score_all, dev.sms, stream);
   if (rc) return rc;
   if (a->ev_after_score) {
@@ -407,6 +438,7 @@ int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, 
   uint32_t* hist = ws_hist(workspace);
   rc = prepare_hist(workspace, a->rows, stream);
   if (rc) return rc;
+  if (!a->logits_out) forget_sentinel(workspace);
   rc = run_scoring(a, logits, hist, status, true, dev.sms, stream);
   if (rc) return rc;
   if (a->ev_after_score) {

@@ -4,41 +4,41 @@
 // The two-launch path (score_kernel, then select_wide_kernel) leaves HBM idle
 // while the selection runs: every scorer CTA's slice spans the whole call, so
 // every row is complete only when the last scorer CTA ends, and only then can
-// the selection of any row start.  Here one grid of two CTAs per SM does both:
+// the selection of any row start.  Here one grid of one CTA per SM does both:
 //
-//   scorer CTAs  the scoring pipeline of score_kernel (TMA producer, one
-//                tcgen05 MMA issuer, four epilogue warps; identical
-//                arithmetic, so the logits are bit-identical), but over an
-//                interleaved schedule: the flat tile sequence is cut into
-//                chunks of `chunk` tiles and scorer s takes chunks
-//                s, s + S, s + 2S, ...  All scorers move through the sequence
-//                together, so rows complete one after another during the
-//                call instead of all at its end.  Rows are laid out longest
-//                first (up to 256 rows), so the rows that complete last are
-//                the cheapest to select.  Each epilogue warp counts the
-//                tiles it finished per row; the warp whose count completes a
-//                row (fence, then an atomic on the row's counter) appends the
-//                row to a completion queue in the workspace.
-//   selector CTAs  take queue entries in order (one atomic per entry), wait
-//                for the entry to be filled (bounded), and run the exact
-//                radix top-2048 of select_wide_kernel on 192 threads over the
-//                row's logits and first-digit histogram, which the L2 holds.
-//                They also write the rows that fit in the top-K and clear the
-//                row's histogram, counter and queue slot for the next call.
+//   scorer CTAs   two independent copies of score_kernel's pipeline per CTA
+//                 (per copy: TMA producer warp, one tcgen05 MMA issuer, four
+//                 epilogue warps, a 5-stage K ring and 256 TMEM columns;
+//                 identical arithmetic, so the logits are bit-identical), over
+//                 an interleaved schedule: the flat tile sequence is cut into
+//                 chunks of `chunk` tiles and pipeline s of S takes chunks
+//                 s, s + S, s + 2S, ...  All pipelines move through the
+//                 sequence together, so rows complete one after another during
+//                 the call.  Rows are laid out longest first (up to 256 rows):
+//                 the rows that complete last are the cheapest to select.  An
+//                 epilogue warp adds the tiles it finished to its row's
+//                 counter with a fire-and-forget reduction when it leaves the
+//                 row (no fence on the scoring path).
+//   selector CTAs a whole SM each (384 threads, the shared memory of both
+//                 pipelines): they take rows in the scoring order (one atomic
+//                 per row), wait for the row's counter to reach its total,
+//                 and run the exact radix top-2048 of select_wide_kernel over
+//                 the row's histogram and logits, which the L2 holds.
+//                 Because the scorers publish without fences, a selector
+//                 checks the data itself: the histogram must sum to the row's
+//                 length (every reduction landed) and no logit may still hold
+//                 the sentinel bit pattern the logits buffer is filled with
+//                 between calls (every store landed); it re-reads otherwise.
+//                 It writes the sentinel back over the row's logits, and
+//                 clears the row's histogram and counter for the next call.
+//                 Selectors also write the rows that fit in the top-K.
 //
-// Opt-in (DSAI_FUSED=1 in the environment): measured on config 1 it is
-// slower than the two-launch path (80 against 42.5 us per call with 32
-// selectors and 8-tile chunks): a 192-thread selector needs ~17 us per row
-// while HBM is saturated (digit 1 ~3 us, the pass over the row's logits
-// ~9.6 us at ~8 GB/s per CTA), and the per-row completion fences and weight
-// reloads slow the interleaved scorers (epilogue warps ~4 us in fences per
-// CTA; the MMA issuer then waits ~12 us for free accumulators).
+// Scorers never wait for selectors; selectors wait (bounded) only for rows
+// that scorers, all resident or scheduled as soon as any CTA retires, will
+// finish.  The row-claim and exit counters live in the workspace header and
+// are reset by the last selector to leave.
 //
-// Scorers never wait for selectors, so the only cross-CTA waits are
-// selectors waiting for rows that scorers (all resident, or scheduled as
-// soon as any CTA retires) will finish; every such wait is bounded.  The
-// queue's head, tail and exit counters live in the workspace header and are
-// reset by the last selector to leave.
+// Opt-in (DSAI_FUSED=1 in the environment).
 #include <cstdlib>
 
 #include "common.cuh"
@@ -53,61 +53,65 @@ namespace {
 using namespace sm100;
 using namespace radix;
 
-constexpr int kFCtasPerSm = 2;
-constexpr int kFThreads = 192;
+constexpr int kFThreads = 384;               // two scoring pipelines of 6 warps
+constexpr int kFPipes = 2;
+constexpr int kFPipeWarps = 6;
 constexpr int kFStages = 5;
-constexpr int kFScaleSlots = 12;  // > 9: the producer runs at most 5 K stages + 4 accumulators ahead of the epilogue
+constexpr int kFScaleSlots = 12;             // > 9: producer runs <= 5 K stages + 4 accumulators ahead
 constexpr int kFAccs = 4;
 constexpr int kFAccCols = kHeads;
-constexpr int kFTmemCols = kFAccs * kFAccCols;
-constexpr int kFEpiThreads = 128;
+constexpr int kFPipeTmemCols = kFAccs * kFAccCols;       // 256 per pipeline
+constexpr int kFTmemCols = kFPipes * kFPipeTmemCols;     // 512
+constexpr int kFEpiWarps = 4;
 constexpr uint32_t kFScaleTx = kPage * 4;
 constexpr int kFSortRows = 256;              // rows laid out longest first up to this many
-constexpr int kFMaxPer = (kMaxRowsPerLaunch + kFThreads - 1) / kFThreads;  // row-table positions per thread
+constexpr int kFMaxPer = (kMaxRowsPerLaunch + kFThreads - 1) / kFThreads;
 
-// Selector shape: 32 entries per thread and round (one mask bit each), three
-// rounds of logits in flight (a ring of shared-memory buffers).
+// Selector shape: 32 entries per thread and round, two rounds in flight.
 constexpr int kFPer = 32;
-constexpr int kFRound = kFThreads * kFPer;   // 6144 entries per round
-constexpr int kFRing = 3;
-constexpr int kFCap = kSplitCap;             // pivot-bin keys kept (the row's list in the workspace)
+constexpr int kFRound = kFThreads * kFPer;   // 12288 entries (48 KB) per round
+constexpr int kFRing = 2;
+constexpr int kFCap = 8192;                  // pivot-bin keys kept in shared memory
 constexpr int kFBtCache = 2048;              // block-table entries of a row in smem (131072 tokens)
-constexpr int kFSmall = 64;                  // second-digit bin small enough to rank directly
-constexpr int kFHistThreads = kHistBins / 32;  // 128 threads own 32 first-digit bins each
-constexpr int kFB2Threads = kBins2 / 8;        // 128 threads own 8 second-digit bins each
+constexpr int kFSmall = 64;
+constexpr int kFH1Threads = 256;             // 16 first-digit bins each
+constexpr int kFH2Threads = 256;             // 4 second-digit bins each
+
+// Logits buffer contents between calls: this bit pattern (a NaN arithmetic
+// never produces on this GPU; the scorer maps it to another NaN) marks
+// entries not yet written by the current call.
+constexpr uint32_t kSentinel = 0xFFFFFFFFu;
 
 // Control words in the workspace header (int offsets, 64 B apart; the status
-// word is int 0): next queue entry to take, entries appended, selectors done.
+// word is int 0): next row position to take, selectors done.
 constexpr int kCtlHead = 16;
-constexpr int kCtlTail = 32;
 constexpr int kCtlFin = 48;
-// Per-row words after the row's 4096 histogram bins: warp-tiles finished
-// (4 epilogue warps x the row's tiles when complete), and queue slot: entry
-// i of the completion queue lives in row i's block (row + 1, 0 = empty).
+// Per-row word after the row's 4096 histogram bins: warp-tiles finished
+// (4 epilogue warps x the row's tiles when complete).
 constexpr int kRowDone = kHistBins + 2;
-constexpr int kRowQueue = kHistBins + 3;
 
 struct FusedParams {
   const float* weights;
   const int32_t* seq_lens;
   const int32_t* block_table;
-  float* logits;
-  uint32_t* hist;     // [rows, kHistStride]: bins zero, counters zero, queue slots zero on entry
-  uint32_t* cand;     // [rows, 2, kSplitCap]: each row's pivot-bin list (keys, then ids)
-  int* ws;            // workspace header: status word, queue control words
+  float* logits;      // sentinel-filled on entry; left so (unless keep_logits)
+  uint32_t* hist;     // [rows, kHistStride]: bins and counters zero on entry, left zero
+  int* ws;            // workspace header: status word, control words
   int32_t* out_ids;
   int rows;
   int max_pages;
   int num_pages;
   int ld;
   int score_all;
+  int keep_logits;    // 1: leave the logits (a caller's buffer), 0: restore the sentinel
   int scorers;        // CTAs [0, scorers) score, the others select
   int chunk;          // tiles per chunk of the interleaved schedule
 };
 
-struct ScorerSmem {
+struct alignas(1024) PipeSmem {
   uint8_t k[kFStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
   uint8_t q[2][kQBytes];
+  float w[2][kHeads];                    // the row's head weights, with its query
   float scale[kFScaleSlots][kTileTok];
   uint64_t full[kFStages];
   uint64_t empty[kFStages];
@@ -118,14 +122,15 @@ struct ScorerSmem {
   uint64_t tfull[kFAccs];
   uint64_t tempty[kFAccs];
   uint64_t drain;
-  uint32_t tmem_base;
   int abort;
 };
 
 struct SelectorSmem {
-  float4 vals[kFRing][kFPer / 4][kFThreads];  // three rounds of logits
-  uint32_t hist[kBins2];              // second (then third) digit histogram
-  int32_t bt[kFBtCache];              // the row's pages
+  float4 vals[kFRing][kFPer / 4][kFThreads];  // two rounds of logits
+  uint32_t cand_key[kFCap];                   // keys in the pivot bin and their ids
+  int32_t cand_val[kFCap];
+  uint32_t hist[kBins2];                      // second (then third) digit histogram
+  int32_t bt[kFBtCache];                      // the row's pages
   uint32_t small_key[kFSmall];
   int32_t small_val[kFSmall];
   Scan sc;
@@ -133,37 +138,36 @@ struct SelectorSmem {
   int cand_count;
   int small_count;
   int eq_count;
-  int extreme[2];                     // first-digit bins 0 and 4088..4095 are not empty
-  int item;                           // the row taken from the queue (-1: none left)
-  int nq;                             // rows that go through the queue
-  int wsum[kFThreads / 32];
+  int extreme[2];                             // first-digit bins 0 and 4088..4095 are not empty
+  int item;                                   // the row taken (-1: none left)
+  int hist_done;
 };
 
 struct FusedSmem {
   union {
-    ScorerSmem sc;
+    PipeSmem pipe[kFPipes];
     SelectorSmem se;
   } u;
+  uint32_t tmem_base;
   int warp_sums[kFThreads / 32];
   uint16_t order[kMaxRowsPerLaunch];      // row of each position of the tile sequence
   int row_start[kMaxRowsPerLaunch + 1];   // first tile of each position
 };
 
 constexpr int kFSmemBytes = static_cast<int>(sizeof(FusedSmem)) + 1024;
-// Two CTAs per SM: no more shared memory than the per-row scorer, which
-// runs two per SM.
-static_assert(kFCtasPerSm * (kFSmemBytes + 1024) <= 226304, "two fused CTAs per SM must fit");
-static_assert(kFHistThreads <= kFThreads && kFB2Threads <= kFThreads, "bin ownership");
-static_assert(kFSmall <= kFThreads, "one thread ranks each small key");
-static_assert(kFPer / 4 == 8, "eight cp.async groups per round");
+static_assert(kFSmemBytes <= 232448, "one fused CTA per SM must fit");
+static_assert(sizeof(PipeSmem) % 1024 == 0, "both pipelines' K rings 1024-B aligned");
+static_assert(kFH1Threads * 16 == kHistBins && kFH2Threads * 4 == kBins2, "bin ownership");
+static_assert(kFSmall <= kFThreads && kFH1Threads <= kFThreads, "selector shape");
+static_assert(kFPer / 4 == 8, "eight float4 per thread and round");
 
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_gpu(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ void fail(ScorerSmem& s, int* status) {
+__device__ __forceinline__ void fail(PipeSmem& s, int* status) {
   report(status, DSAI_STATUS_WAIT_TIMEOUT);
   *reinterpret_cast<volatile int*>(&s.abort) = 1;
 }
@@ -221,8 +225,8 @@ __device__ void build_order(FusedSmem& s, const FusedParams& p) {
   __syncthreads();
 }
 
-// The tiles of scorer s of S: chunks s, s + S, ... of `chunk` tiles each over
-// the T tiles of the sequence; local tile j is global tile tile(j).
+// The tiles of pipeline s of S: chunks s, s + S, ... of `chunk` tiles each
+// over the T tiles of the sequence; local tile j is global tile tile(j).
 struct Sched {
   int s, S, C, n;
   __device__ void init(int s_, int S_, int C_, int T) {
@@ -237,7 +241,7 @@ struct Sched {
   __device__ __forceinline__ int tile(int j) const { return ((j / C) * S + s) * C + (j % C); }
 };
 
-// Walks a scorer's tiles: the position of the tile's row in the sequence,
+// Walks a pipeline's tiles: the position of the tile's row in the sequence,
 // the tile's index inside the row, the row's end.
 struct FCursor {
   int j, t, pos, jr, end;
@@ -283,16 +287,19 @@ __device__ __forceinline__ TileRef resolve_tile(const FusedSmem& s, const FusedP
 
 // ---------------------------------------------------------------- scorer
 
-__device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUtensorMap* tmap_k,
-                            const CUtensorMap* tmap_s, const FusedParams& p) {
-  ScorerSmem& s = sm.u.sc;
+// One scoring pipeline: warps [6*pipe, 6*pipe + 6) of the CTA, its own
+// shared memory and TMEM columns, scoring pipeline index `gp` of `npipes`.
+__device__ void pipe_role(FusedSmem& sm, PipeSmem& s, uint32_t tmem, const CUtensorMap* tmap_q,
+                          const CUtensorMap* tmap_k, const CUtensorMap* tmap_s, const FusedParams& p,
+                          int gp, int npipes) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int role = warp % kFPipeWarps;
   const int* rs = sm.row_start;
   Sched sched;
-  sched.init(blockIdx.x, p.scorers, p.chunk, rs[p.rows]);
+  sched.init(gp, npipes, p.chunk, rs[p.rows]);
   if (sched.n <= 0) return;
 
-  if (warp == 0) {
+  if (role == 0) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_k = l2_policy_evict_first();
     const uint64_t pol_q = l2_policy_evict_last();
@@ -322,13 +329,17 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
           if (ps != cur_pos) {
             cur_pos = ps;
             qs ^= 1;
+            // The slot is free once the MMAs of its last row completed and
+            // every epilogue warp took that row's weights.
             if (!mbar_wait(&s.qempty[qs], qe_par[qs] ^ 1u, &s.abort, kWaitTimeoutNs)) {
               good = 0;
             } else {
               qe_par[qs] ^= 1u;
               ++q_uses[qs];
-              mbar_arrive_expect_tx(&s.qfull[qs], kQBytes);
-              tma_load_2d(s.q[qs], tmap_q, &s.qfull[qs], 0, static_cast<int>(sm.order[ps]) * kHeads, pol_q);
+              const int row = sm.order[ps];
+              mbar_arrive_expect_tx(&s.qfull[qs], kQBytes + kHeads * 4);
+              tma_load_2d(s.q[qs], tmap_q, &s.qfull[qs], 0, row * kHeads, pol_q);
+              bulk_load(s.w[qs], p.weights + static_cast<size_t>(row) * kHeads, kHeads * 4, &s.qfull[qs], pol_q);
             }
           }
           if (good && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs)) good = 0;
@@ -371,7 +382,7 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
           report(p.ws, DSAI_STATUS_WAIT_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (role == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc_e4m3_f32(kTileTok, kHeads);
@@ -393,7 +404,7 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
         tc_fence_after();
         const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.k[stage]));
         const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.q[qs]));
-        const uint32_t d = s.tmem_base + static_cast<uint32_t>(acc * kFAccCols);
+        const uint32_t d = tmem + static_cast<uint32_t>(acc * kFAccCols);
 #pragma unroll
         for (int kk = 0; kk < kDim / 32; ++kk)  // K = 32 e4m3 (32 B) per MMA
           umma_f8(d, adesc + 2u * kk, bdesc + 2u * kk, idesc, kk > 0 ? 1u : 0u);
@@ -410,31 +421,19 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;              // TMEM lanes [32*quad, 32*quad+32)
     const int tok = quad * 32 + lane;       // token of the tile owned by this thread
-    int acc = 0, sslot = 0, cur_pos = -1, cur_row = 0, L = 0, pending = 0;
+    int acc = 0, sslot = 0, qs = 1, cur_pos = -1, cur_row = 0, L = 0, pending = 0;
     uint32_t aphase = 0, sphase = 0;
+    uint32_t qf_par[2] = {0u, 0u};
     bool hist_row = false;
     float w[kHeads];
     float* out_row = nullptr;
     uint32_t* hist_g = nullptr;
-    // Publishes this warp's finished tiles of the current row: the warp's
-    // logits and histogram additions are fenced before its count; the warp
-    // whose count completes the row appends the row to the queue.
+    // Publishes this warp's finished tiles of the current row (no fence: a
+    // selector checks that the row's data landed before it uses it).
     auto flush = [&]() {
       if (hist_row && pending > 0) {
-        __threadfence();
         __syncwarp();
-        if (lane == 0) {
-          const uint32_t total = 4u * static_cast<uint32_t>(rs[cur_pos + 1] - rs[cur_pos]);
-          const uint32_t old = atomicAdd(hist_g + kRowDone, static_cast<uint32_t>(pending));
-          if (old + static_cast<uint32_t>(pending) == total) {
-            __threadfence();
-            const int qpos = atomicAdd(p.ws + kCtlTail, 1);
-            if (qpos >= 0 && qpos < p.rows)
-              atomicExch(p.hist + static_cast<size_t>(qpos) * kHistStride + kRowQueue,
-                         static_cast<uint32_t>(cur_row + 1));
-          }
-        }
-        __syncwarp();
+        if (lane == 0) atomicAdd(hist_g + kRowDone, static_cast<uint32_t>(pending));  // RED
       }
       pending = 0;
     };
@@ -446,12 +445,23 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
         flush();
         cur_pos = c.pos;
         cur_row = sm.order[cur_pos];
-        const float4* w4 = reinterpret_cast<const float4*>(p.weights + static_cast<size_t>(cur_row) * kHeads);
+        qs ^= 1;
+        // The row's weights came with its query (the MMA issuer saw the slot
+        // fill; this wait makes the copy visible to this warp too).
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.qfull[qs], qf_par[qs], &s.abort, kWaitTimeoutNs))) {
+          fail(s, p.ws);
+          ok = false;
+          break;
+        }
+        qf_par[qs] ^= 1u;
+        const float4* w4 = reinterpret_cast<const float4*>(s.w[qs]);
 #pragma unroll
         for (int i = 0; i < kHeads / 4; ++i) {
-          const float4 v = __ldg(w4 + i);
+          const float4 v = w4[i];
           w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.qempty[qs]);
         L = row_len(p.seq_lens, cur_row, p.max_pages, nullptr);
         hist_row = L > kTopK;  // only rows that go through the radix select
         out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
@@ -464,8 +474,7 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
       }
       tc_fence_after();
       uint32_t r0[32], r1[32];
-      const uint32_t taddr = s.tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                             static_cast<uint32_t>(acc * kFAccCols);
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * kFAccCols);
       tmem_ld_32x32b_x32(taddr, r0);
       tmem_ld_32x32b_x32(taddr + 32u, r1);
       tmem_wait_ld();
@@ -493,7 +502,8 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
         b2 = fmaf(fmaxf(__uint_as_float(r1[h + 2]), 0.f), w[32 + h + 2], b2);
         b3 = fmaf(fmaxf(__uint_as_float(r1[h + 3]), 0.f), w[32 + h + 3], b3);
       }
-      const float logit = (((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3))) * sc;
+      float logit = (((a0 + b0) + (a1 + b1)) + ((a2 + b2) + (a3 + b3))) * sc;
+      if (__float_as_uint(logit) == kSentinel) logit = __uint_as_float(0x7FFFFFFFu);
       const int t_abs = c.jr * kTileTok + tok;
       const bool live = t_abs < L;
       if (live) out_row[t_abs] = logit;
@@ -515,30 +525,45 @@ __device__ void scorer_role(FusedSmem& sm, const CUtensorMap* tmap_q, const CUte
 
 // ---------------------------------------------------------------- selector
 
+// A float4 of the row's logits whose valid entries (mask bits) still hold
+// the sentinel is re-read from L2 until every valid entry has landed
+// (bounded; false on timeout).
+__device__ __forceinline__ bool settle(float4& w, const float* src, uint32_t valid) {
+  auto waiting = [&](const float4& v) {
+    return ((valid & 1u) && __float_as_uint(v.x) == kSentinel) || ((valid & 2u) && __float_as_uint(v.y) == kSentinel) ||
+           ((valid & 4u) && __float_as_uint(v.z) == kSentinel) || ((valid & 8u) && __float_as_uint(v.w) == kSentinel);
+  };
+  if (!waiting(w)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    w = __ldcg(reinterpret_cast<const float4*>(src));
+    if (!waiting(w)) return true;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+}
+
 // The exact top-2048 of one completed row (kIds form of select_wide_kernel,
-// 192 threads): digit 1 from the row's histogram, one pass over the logits
+// 384 threads): digit 1 from the row's histogram, one pass over the logits
 // (keys above the pivot bin to the output, keys in it to a list and the
 // second-digit histogram), then digits 2 and 3 over the list.  Clears the
-// row's histogram and completion counter.
+// row's histogram and counter; restores the sentinel over its logits.
 __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int L = row_len(p.seq_lens, b, p.max_pages, nullptr);
   const int32_t* bt_row = p.block_table + static_cast<size_t>(b) * p.max_pages;
-  const float* row = p.logits + static_cast<size_t>(b) * p.ld;
+  float* row = p.logits + static_cast<size_t>(b) * p.ld;
   RowOut<true> out;
   out.ids = p.out_ids + static_cast<size_t>(b) * kTopK;
   out.scores = nullptr;
   out.tokens = nullptr;
   out.offset = 0;
   uint32_t* g_hist = p.hist + static_cast<size_t>(b) * kHistStride;
-  uint32_t* list_key = p.cand + static_cast<size_t>(b) * 2 * kSplitCap;
-  int32_t* list_val = reinterpret_cast<int32_t*>(list_key + kSplitCap);
   if (tid == 0) {
     s.out_count = 0;
     s.cand_count = 0;
     s.small_count = 0;
     s.eq_count = 0;
-    g_hist[kRowDone] = 0u;  // every count of this row has arrived
   }
   const int npg = (L + kPage - 1) / kPage;
   const bool bt_cached = npg <= kFBtCache;
@@ -546,19 +571,9 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
     for (int i = tid; i < npg; i += kFThreads) s.bt[i] = bt_row[i];
   for (int i = tid; i < kBins2; i += kFThreads) s.hist[i] = 0u;
 
-  // Digit 1: threads < 128 own 32 bins each, read from L2 (other SMs wrote them).
-  uint32_t h1[32];
-  uint4* g4 = reinterpret_cast<uint4*>(g_hist) + tid * 8;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint4 v = tid < kFHistThreads ? __ldcg(g4 + k) : make_uint4(0u, 0u, 0u, 0u);
-    h1[4 * k] = v.x; h1[4 * k + 1] = v.y; h1[4 * k + 2] = v.z; h1[4 * k + 3] = v.w;
-  }
-
   // Round r of logits (entries [r*kFRound, (r+1)*kFRound)) into ring slot
-  // r % kFRing (L2 only: cp.async.cg), one cp.async group per round; each
-  // thread reads only its own entries, so it waits only for its own copies.
-  // Entries past the row's end are zero-filled without reading.
+  // r % kFRing (L2 only), one cp.async group per round; each thread reads
+  // only its own entries.  Entries past the row's end are zero-filled.
   const int nrounds = (L + kFRound - 1) / kFRound;
   auto load_round = [&](int r) {
     const int base = r * kFRound;
@@ -574,18 +589,50 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
 #pragma unroll
   for (int r = 0; r < kFRing; ++r) load_round(r);
 
+  // Digit 1: threads < 256 own 16 bins each, read from L2.  The bins must
+  // add up to the row's length: reductions still in flight are waited for.
+  uint32_t h1[16];
+  const uint4* g4 = reinterpret_cast<const uint4*>(g_hist) + tid * 4;
+  const uint64_t t_h = global_timer_ns();
+  while (true) {
+    uint32_t part = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint4 v = tid < kFH1Threads ? __ldcg(g4 + k) : make_uint4(0u, 0u, 0u, 0u);
+      h1[4 * k] = v.x; h1[4 * k + 1] = v.y; h1[4 * k + 2] = v.z; h1[4 * k + 3] = v.w;
+      part += v.x + v.y + v.z + v.w;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane == 0) s.sc.warp_tot[warp] = static_cast<int>(part);
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < kFThreads / 32; ++w) t += static_cast<uint32_t>(s.sc.warp_tot[w]);
+      const bool complete = t == static_cast<uint32_t>(L);
+      const bool timeout = !complete && global_timer_ns() - t_h > kWaitTimeoutNs;
+      if (timeout) report(p.ws, DSAI_STATUS_WAIT_TIMEOUT);
+      s.hist_done = (complete || timeout) ? 1 : 0;
+    }
+    __syncthreads();
+    if (s.hist_done) break;
+    __nanosleep(256);
+  }
+
   if (tid == 0) s.extreme[0] = h1[0] != 0u;
-  if (tid == kFHistThreads - 1) {
+  if (tid == kFH1Threads - 1) {
     uint32_t x = 0u;
 #pragma unroll
-    for (int i = 24; i < 32; ++i) x |= h1[i];
+    for (int i = 8; i < 16; ++i) x |= h1[i];
     s.extreme[1] = x != 0u;
   }
-  find_threshold<kFThreads, 32>(s.sc, h1, kTopK);  // its barriers publish the zeroed counters
-  if (tid < kFHistThreads) {
+  find_threshold<kFThreads, 16>(s.sc, h1, kTopK);  // its barriers publish the zeroed counters
+  if (tid < kFH1Threads) {
+    uint4* gz = reinterpret_cast<uint4*>(g_hist) + tid * 4;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) __stcg(g4 + k, make_uint4(0u, 0u, 0u, 0u));  // clean for the next call
+    for (int k = 0; k < 4; ++k) __stcg(gz + k, make_uint4(0u, 0u, 0u, 0u));  // clean for the next call
   }
+  if (tid == 0) g_hist[kRowDone] = 0u;
   const uint32_t bin1 = static_cast<uint32_t>(s.sc.sel_bin);
   const int above1 = s.sc.sel_above;
   const int n1 = s.sc.sel_count;
@@ -601,6 +648,7 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
     return page * kPage + (i & (kPage - 1));
   };
 
+  bool landed = true;
   for (int r = 0; r < nrounds; ++r) {
     const int base = r * kFRound;
     float4(*vals)[kFThreads] = s.vals[r % kFRing];
@@ -610,7 +658,13 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
 #pragma unroll
     for (int u = 0; u < kFPer / 4; ++u) {
       if (u < groups) {
-        const float4 w = vals[u][tid];
+        const int left = L - (base + 4 * (u * kFThreads + tid));
+        const uint32_t valid = left >= 4 ? 0xFu : (left > 0 ? (1u << left) - 1u : 0u);
+        float4 w = vals[u][tid];
+        if (valid) {
+          if (!settle(w, row + base + 4 * (u * kFThreads + tid), valid)) landed = false;
+          vals[u][tid] = w;
+        }
         if (fast_skip && fmaxf(fmaxf(w.x, w.y), fmaxf(w.z, w.w)) < f_lo) continue;
         const uint32_t k4[4] = {key_of_bits(__float_as_uint(w.x)), key_of_bits(__float_as_uint(w.y)),
                                 key_of_bits(__float_as_uint(w.z)), key_of_bits(__float_as_uint(w.w))};
@@ -620,12 +674,8 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
           g |= static_cast<uint32_t>(k4[c] > key_top) << c;
           n |= static_cast<uint32_t>(k4[c] >= key_lo) << c;
         }
-        if (u == groups - 1) {  // entries at or past L
-          const int left = L - (base + 4 * (u * kFThreads + tid));
-          const uint32_t valid = left >= 4 ? 0xFu : (left > 0 ? (1u << left) - 1u : 0u);
-          g &= valid;
-          n &= valid;
-        }
+        g &= valid;
+        n &= valid;
         gtm |= g << (4 * u);
         inm |= n << (4 * u);
       }
@@ -645,8 +695,8 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
       const int e = __ffs(m) - 1;
       const uint32_t key = key_of_entry(e);
       if (cpos < kFCap) {
-        list_key[cpos] = key;
-        list_val[cpos] = value_of(entry(e));
+        s.cand_key[cpos] = key;
+        s.cand_val[cpos] = value_of(entry(e));
       }
       ++cpos;
       atomicAdd(&s.hist[(key >> 10) & (kBins2 - 1)], 1u);
@@ -654,11 +704,12 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
     load_round(r + kFRing);  // refill this slot (this thread's entries only)
   }
   cp_async_wait_group<0>();
+  if (!landed) report(p.ws, DSAI_STATUS_WAIT_TIMEOUT);
   __syncthreads();  // candidates, second-digit counts and output slots are final
 
   if (!listed) {
     // More keys in the pivot bin than the list holds: the second digit over
-    // the row in global memory.
+    // the row in global memory (every entry has landed by now).
     for (int base = 0; base < L; base += kFThreads) {
       const int i = base + tid;
       const uint32_t key = i < L ? ordered_key(__ldcg(row + i)) : 0u;
@@ -666,10 +717,10 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
     }
     __syncthreads();
   }
-  uint32_t h2[8];
+  uint32_t h2[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) h2[i] = tid < kFB2Threads ? s.hist[8 * tid + i] : 0u;
-  find_threshold<kFThreads, 8>(s.sc, h2, k1);
+  for (int i = 0; i < 4; ++i) h2[i] = tid < kFH2Threads ? s.hist[4 * tid + i] : 0u;
+  find_threshold<kFThreads, 4>(s.sc, h2, k1);
   const uint32_t prefix2 = (bin1 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
   const int k2 = k1 - s.sc.sel_above;  // keys still needed from the second-digit bin
   const int n2 = s.sc.sel_count;
@@ -677,17 +728,16 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
 
   const int n3 = listed ? min(s.cand_count, kFCap) : L;
   auto key_at = [&](int j) -> uint32_t {
-    if (listed) return __ldcg(list_key + j);
+    if (listed) return s.cand_key[j];
     const uint32_t key = ordered_key(__ldcg(row + j));
     return (key >> (32 - kHistBits)) == bin1 ? key : 0u;
   };
   auto val_at = [&](int j) -> int32_t {
-    if (listed) return __ldcg(list_val + j);
+    if (listed) return s.cand_val[j];
     return physical_id(bt_row, j);
   };
 
   if (small) {
-    // Emit the keys above the 22-bit prefix; collect the prefix's keys.
     for (int base = 0; base < n3; base += kFThreads) {
       const int j = base + tid;
       const uint32_t key = j < n3 ? key_at(j) : 0u;
@@ -703,8 +753,6 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
       }
     }
     __syncthreads();
-    // Rank the n2 keys (largest first, ties by list position): one thread
-    // per key; the k2 best take the last k2 slots.
     const int n = min(s.small_count, kFSmall);
     if (tid < n) {
       const uint32_t ki = s.small_key[tid];
@@ -715,52 +763,47 @@ __device__ void select_row(SelectorSmem& s, const FusedParams& p, int b) {
       }
       if (r < k2) out.emit(kTopK - k2 + r, s.small_val[tid], ki);
     }
-    return;
-  }
-
-  // Many keys share the 22-bit prefix: count the third digit over them.
-  for (int i = tid; i < kBins2; i += kFThreads) s.hist[i] = 0u;
-  __syncthreads();
-  for (int base = 0; base < n3; base += kFThreads) {
-    const int j = base + tid;
-    const uint32_t key = j < n3 ? key_at(j) : 0u;
-    if (j < n3 && key != 0u && (key >> 10) == prefix2) atomicAdd(&s.hist[key & (kBins2 - 1)], 1u);
-  }
-  __syncthreads();
-  uint32_t h3[8];
+  } else {
+    // Many keys share the 22-bit prefix: count the third digit over them.
+    for (int i = tid; i < kBins2; i += kFThreads) s.hist[i] = 0u;
+    __syncthreads();
+    for (int base = 0; base < n3; base += kFThreads) {
+      const int j = base + tid;
+      const uint32_t key = j < n3 ? key_at(j) : 0u;
+      if (j < n3 && key != 0u && (key >> 10) == prefix2) atomicAdd(&s.hist[key & (kBins2 - 1)], 1u);
+    }
+    __syncthreads();
+    uint32_t h3[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) h3[i] = tid < kFB2Threads ? s.hist[8 * tid + i] : 0u;
-  find_threshold<kFThreads, 8>(s.sc, h3, k2);
-  const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
-  const int k3 = k2 - s.sc.sel_above;  // how many keys equal to the pivot are taken
-  for (int base = 0; base < n3; base += kFThreads) {
-    const int j = base + tid;
-    const uint32_t key = j < n3 ? key_at(j) : 0u;
-    const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
-    const bool gt = in && key > pivot;
-    const bool eq = in && key == pivot;
-    const int pos = warp_alloc_1(&s.out_count, gt);
-    const int ticket = warp_alloc_1(&s.eq_count, eq);
-    if (gt) out.emit(pos, val_at(j), key);
-    if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
+    for (int i = 0; i < 4; ++i) h3[i] = tid < kFH2Threads ? s.hist[4 * tid + i] : 0u;
+    find_threshold<kFThreads, 4>(s.sc, h3, k2);
+    const uint32_t pivot = (prefix2 << 10) | static_cast<uint32_t>(s.sc.sel_bin);
+    const int k3 = k2 - s.sc.sel_above;  // how many keys equal to the pivot are taken
+    for (int base = 0; base < n3; base += kFThreads) {
+      const int j = base + tid;
+      const uint32_t key = j < n3 ? key_at(j) : 0u;
+      const bool in = j < n3 && key != 0u && (key >> (32 - kHistBits)) == bin1;
+      const bool gt = in && key > pivot;
+      const bool eq = in && key == pivot;
+      const int pos = warp_alloc_1(&s.out_count, gt);
+      const int ticket = warp_alloc_1(&s.eq_count, eq);
+      if (gt) out.emit(pos, val_at(j), key);
+      if (eq && ticket < k3) out.emit(kTopK - k3 + ticket, val_at(j), key);
+    }
+  }
+  __syncthreads();  // every read of the row's logits is done
+  if (!p.keep_logits) {
+    // The sentinel back over the row's logits, for the next call.
+    const float4 sent = make_float4(__uint_as_float(kSentinel), __uint_as_float(kSentinel),
+                                    __uint_as_float(kSentinel), __uint_as_float(kSentinel));
+    float4* r4 = reinterpret_cast<float4*>(row);
+    for (int i = tid; i < (L + 3) / 4; i += kFThreads) __stcg(r4 + i, sent);
   }
 }
 
 __device__ void selector_role(FusedSmem& sm, const FusedParams& p, int sel, int nsel) {
   SelectorSmem& s = sm.u.se;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // Rows through the queue: those longer than the top-K.
-  int cnt = 0;
-  for (int b = tid; b < p.rows; b += kFThreads) cnt += row_len(p.seq_lens, b, p.max_pages, nullptr) > kTopK;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
-  if (lane == 0) s.wsum[warp] = cnt;
-  __syncthreads();
-  if (tid == 0) {
-    int t = 0;
-    for (int w = 0; w < kFThreads / 32; ++w) t += s.wsum[w];
-    s.nq = t;
-  }
+  const int tid = threadIdx.x;
   // Rows that fit in the top-K: every token in order, -1 padding
   // (reference kernel.cu:897-905), spread over the selectors.
   for (int b = sel; b < p.rows; b += nsel) {
@@ -770,30 +813,33 @@ __device__ void selector_role(FusedSmem& sm, const FusedParams& p, int sel, int 
     int32_t* o = p.out_ids + static_cast<size_t>(b) * kTopK;
     for (int i = tid; i < kTopK; i += kFThreads) o[i] = i < L ? physical_id(bt_row, i) : -1;
   }
-  __syncthreads();
-  const int nq = s.nq;
+  // The other rows, in the order they are scored: take a position, wait for
+  // its row's tiles, select.
   while (true) {
     if (tid == 0) {
-      const int my = atomicAdd(p.ws + kCtlHead, 1);
       int item = -1;
-      if (my < nq) {
-        uint32_t* slot = p.hist + static_cast<size_t>(my) * kHistStride + kRowQueue;
-        uint32_t v = ld_acquire_gpu(slot);
-        if (v == 0u) {
+      while (true) {
+        const int k = atomicAdd(p.ws + kCtlHead, 1);
+        if (k >= p.rows) break;
+        const int b = sm.order[k];
+        if (row_len(p.seq_lens, b, p.max_pages, nullptr) <= kTopK) continue;  // written above
+        const uint32_t total = 4u * static_cast<uint32_t>(sm.row_start[k + 1] - sm.row_start[k]);
+        const uint32_t* done = p.hist + static_cast<size_t>(b) * kHistStride + kRowDone;
+        uint32_t v = ld_relaxed_gpu(done);
+        if (v != total) {
           const uint64_t t0 = global_timer_ns();
           uint32_t n = 0;
-          while ((v = ld_acquire_gpu(slot)) == 0u) {
+          while ((v = ld_relaxed_gpu(done)) != total) {
             __nanosleep(128);
             if ((++n & 15u) == 0u && global_timer_ns() - t0 > kWaitTimeoutNs) break;
           }
         }
-        if (v != 0u && static_cast<int>(v) <= p.rows) {
-          *slot = 0u;  // clean for the next call
-          __threadfence();
-          item = static_cast<int>(v) - 1;
+        if (v == total) {
+          item = b;
         } else {
           report(p.ws, DSAI_STATUS_WAIT_TIMEOUT);
         }
+        break;
       }
       s.item = item;
     }
@@ -804,18 +850,17 @@ __device__ void selector_role(FusedSmem& sm, const FusedParams& p, int sel, int 
     __syncthreads();
   }
   if (tid == 0) {
-    // The last selector to leave resets the queue for the next call: every
-    // selector took its last entry, so every row was appended and taken.
+    // The last selector to leave resets the claim counter for the next call:
+    // every selector has taken its last position.
     const int f = atomicAdd(p.ws + kCtlFin, 1);
     if (f == nsel - 1) {
       atomicExch(p.ws + kCtlHead, 0);
-      atomicExch(p.ws + kCtlTail, 0);
       atomicExch(p.ws + kCtlFin, 0);
     }
   }
 }
 
-__global__ void __launch_bounds__(kFThreads, kFCtasPerSm)
+__global__ void __launch_bounds__(kFThreads, 1)
     fused_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                  const __grid_constant__ CUtensorMap tmap_s, const FusedParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -823,55 +868,55 @@ __global__ void __launch_bounds__(kFThreads, kFCtasPerSm)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool scorer = static_cast<int>(blockIdx.x) < p.scorers;
-  ScorerSmem& s = sm.u.sc;
+  const int pipe = warp / kFPipeWarps;
 
   // Shared memory and kernel parameters only before the programmatic wait.
-  if (scorer && tid == 0) {
+  if (scorer && (warp % kFPipeWarps) == 0 && lane == 0) {
+    PipeSmem& s = sm.u.pipe[pipe];
     for (int i = 0; i < kFStages; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < kFScaleSlots; ++i) {
       mbar_init(&s.sfull[i], 1);
-      mbar_init(&s.sempty[i], kFEpiThreads / 32);
+      mbar_init(&s.sempty[i], kFEpiWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.qfull[i], 1);
-      mbar_init(&s.qempty[i], 1);
+      mbar_init(&s.qempty[i], 1 + kFEpiWarps);  // MMA commit + every epilogue warp
     }
     for (int i = 0; i < kFAccs; ++i) {
       mbar_init(&s.tfull[i], 1);
-      mbar_init(&s.tempty[i], kFEpiThreads / 32);
+      mbar_init(&s.tempty[i], kFEpiWarps);
     }
     mbar_init(&s.drain, 1);
     s.abort = 0;
     fence_mbar_init();
-  }
-  if (scorer && warp == 0 && lane == 0) {
     prefetch_tmap(&tmap_q);
     prefetch_tmap(&tmap_k);
     prefetch_tmap(&tmap_s);
   }
   grid_dep_wait();
   grid_dep_launch_dependents();
+  build_order(sm, p);
   if (!scorer) {
     selector_role(sm, p, static_cast<int>(blockIdx.x) - p.scorers, static_cast<int>(gridDim.x) - p.scorers);
     return;
   }
-  build_order(sm, p);
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, kFTmemCols);
+    tmem_alloc(&sm.tmem_base, kFTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  scorer_role(sm, &tmap_q, &tmap_k, &tmap_s, p);
+  pipe_role(sm, sm.u.pipe[pipe], sm.tmem_base + static_cast<uint32_t>(pipe * kFPipeTmemCols), &tmap_q, &tmap_k,
+            &tmap_s, p, static_cast<int>(blockIdx.x) * kFPipes + pipe, p.scorers * kFPipes);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(s.tmem_base, kFTmemCols);
+    tmem_dealloc(sm.tmem_base, kFTmemCols);
   }
 }
 
@@ -888,6 +933,8 @@ bool fused_enabled() {
   return on != 0;
 }
 
+uint32_t fused_logits_sentinel() { return kSentinel; }
+
 cudaError_t launch_fused(const FusedLaunch& lp, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
                          const CUtensorMap& tmap_s, cudaStream_t stream) {
   static bool attr_set[64] = {};  // the attributes are per function and device
@@ -900,12 +947,10 @@ cudaError_t launch_fused(const FusedLaunch& lp, const CUtensorMap& tmap_q, const
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  // Two CTAs per SM, as the per-row scorer (same shared memory and register
-  // budget; the occupancy query reports one for this kernel, but two are
-  // resident on B200, measured).  Selectors only wait for scorers and
-  // scorers never wait for selectors, so the grid completes even if fewer
-  // CTAs were resident at once.
-  const int grid = kFCtasPerSm * lp.sms;
+  // One CTA per SM.  Selectors only wait for scorers and scorers never wait
+  // for selectors, so the grid completes even if fewer CTAs were resident
+  // at once.
+  const int grid = lp.sms;
   static const int sel_env = env_int("DSAI_FUSED_SELECTORS", 0);
   static const int chunk_env = env_int("DSAI_FUSED_CHUNK", 0);
   int nsel = sel_env > 0 ? sel_env : lp.rows / 4;
@@ -917,7 +962,6 @@ cudaError_t launch_fused(const FusedLaunch& lp, const CUtensorMap& tmap_q, const
   p.block_table = lp.block_table;
   p.logits = lp.logits;
   p.hist = lp.hist;
-  p.cand = lp.cand;
   p.ws = lp.ws;
   p.out_ids = lp.out_ids;
   p.rows = lp.rows;
@@ -925,8 +969,9 @@ cudaError_t launch_fused(const FusedLaunch& lp, const CUtensorMap& tmap_q, const
   p.num_pages = lp.num_pages;
   p.ld = lp.ld;
   p.score_all = lp.score_all;
+  p.keep_logits = lp.keep_logits;
   p.scorers = grid - nsel;
-  p.chunk = chunk_env > 0 ? chunk_env : 4;
+  p.chunk = chunk_env > 0 ? chunk_env : 8;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(kFThreads);

@@ -42,14 +42,14 @@ struct FusedLaunch {
   const int32_t* block_table;
   float* logits;      // [rows, ld]
   uint32_t* hist;     // [rows, kHistStride] (zero on entry, left zero)
-  uint32_t* cand;     // [rows, 2, kSplitCap] pivot-bin lists
-  int* ws;            // workspace header (status word and the queue's control words)
+  int* ws;            // workspace header (status word and the selectors' control words)
   int32_t* out_ids;   // [rows, 2048]
   int rows;           // at most kMaxRowsPerLaunch
   int max_pages;
   int num_pages;
   int ld;
   int score_all;
+  int keep_logits;    // 1: `logits` is the caller's buffer (left holding the logits)
   int sms;
 };
 
@@ -58,7 +58,10 @@ struct FusedLaunch {
 // that select each row as soon as its scoring completes.  Opt-in:
 // fused_enabled() is true only with DSAI_FUSED=1 in the environment (it is
 // slower than the two-launch path on the benchmark shapes).
+// `logits` must hold fused_logits_sentinel() in every 32-bit word the call
+// writes (rows x seq_len) on entry; without keep_logits the call leaves it so.
 bool fused_enabled();
+uint32_t fused_logits_sentinel();
 cudaError_t launch_fused(const FusedLaunch& p, const CUtensorMap& tmap_q, const CUtensorMap& tmap_k,
                          const CUtensorMap& tmap_s, cudaStream_t stream);
 

@@ -572,16 +572,28 @@ def strong_config2(args, world, rank, local) -> dict:
         for _ in range(3):
             D.gather_rows(out, counts, buf=gbuf)
         torch.cuda.synchronize()
+        # device time of the all-gather: 10 calls captured in a CUDA graph
+        ggraph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        dist.barrier()
+        with torch.cuda.graph(ggraph, stream=side):
+            for _ in range(10):
+                D.gather_rows(out, counts, buf=gbuf)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        ggraph.replay()
+        torch.cuda.synchronize()
         dist.barrier()
         g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         g0.record()
-        for _ in range(10):
-            D.gather_rows(out, counts, buf=gbuf)
+        ggraph.replay()
         g1.record()
         torch.cuda.synchronize()
         tg = torch.tensor([g0.elapsed_time(g1) / 10], device=dev)
         dist.all_reduce(tg, op=dist.ReduceOp.MAX)
         gather_us = round(float(tg.item()) * 1e3, 2)
+        dist.barrier()
+        del ggraph  # holds NCCL work: released before the process group
     else:
         counts, gather_us = [r1 - r0], 0.0
     peak, _ = measured_hbm_peak()
@@ -592,6 +604,7 @@ def strong_config2(args, world, rank, local) -> dict:
             "scaling": "strong", "rows_per_rank": counts, "us_per_call": round(per_call * 1e3, 2),
             "value": round(gbs, 1), "unit": "GB/s (whole batch)", "frac_of_n_x_hbm_peak": round(gbs / (world * peak), 4),
             "steps": steps, "gather_rows_us": gather_us,
+            "gather_rows_timing": "10 calls captured in a CUDA graph, replayed once, CUDA events, max over ranks",
             "timing": "CUDA events, max over ranks; each rank holds only its rows' pages; no collective in the timed calls",
             "clocks": clk}
 
@@ -624,13 +637,17 @@ def split_config3(args, world, rank, local, steps: int | None = None) -> dict:
     bt_full = g.block_table[0].contiguous()
     sl_full = g.seq_lens[:1].contiguous()
     out = torch.empty(2048, dtype=torch.int32, device=dev)
+    cand_sc = torch.empty(world * 2048, dtype=torch.float32, device=dev)  # every rank's scores, then tokens
+    cand_tk = torch.empty(world * 2048, dtype=torch.int32, device=dev)
+    ws = _lib.Workspace(dev)  # explicit: the same workspace in eager calls and in the captured graph
 
     def step(i=0):
-        run_pairs(g.q, pools[i % len(pools)], g.weights, sl_local, bt_local, p0 * 64, sc, tk)
+        run_pairs(g.q, pools[i % len(pools)], g.weights, sl_local, bt_local, p0 * 64, sc, tk, workspace=ws)
         if world > 1:
             dist.all_gather_into_tensor(all_pairs.view(-1), pairs.view(-1))
-            merge_pairs(all_pairs[:, 0].reshape(-1).view(torch.float32), all_pairs[:, 1].reshape(-1),
-                        bt_full, sl_full, out)
+            cand_sc.view(world, 2048).copy_(all_pairs[:, 0].view(torch.float32))
+            cand_tk.view(world, 2048).copy_(all_pairs[:, 1])
+            merge_pairs(cand_sc, cand_tk, bt_full, sl_full, out)
         else:
             merge_pairs(sc.view(-1), tk.view(-1), bt_full, sl_full, out)
 
@@ -644,8 +661,24 @@ def split_config3(args, world, rank, local, steps: int | None = None) -> dict:
     got = set(out.tolist())
     if not set(planted) <= got or len(got & set(direct[0].tolist())) < 2048 - 16:
         raise SystemExit(json.dumps({"error": "split-row parity guard failed"}))
-    for _ in range(args.warmup):
-        step()
+    for i in range(max(args.warmup, len(pools))):
+        step(i)
+    torch.cuda.synchronize()
+    # The step as a serving loop runs it: one CUDA graph of one step per pool
+    # copy (16 steps, the NCCL all-gather included), replayed; the per-call
+    # Python and launch work would otherwise dominate this latency-bound step.
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    if world > 1:
+        dist.barrier()
+    with torch.cuda.graph(graph, stream=side):
+        for i in range(len(pools)):
+            step(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    reps = max(1, steps // len(pools))
+    for _ in range(2):
+        graph.replay()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -653,15 +686,22 @@ def split_config3(args, world, rank, local, steps: int | None = None) -> dict:
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for i in range(steps):
-        step(i)
+    for _ in range(reps):
+        graph.replay()
     e1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
+    got_g = set(out.tolist())
+    if not set(planted) <= got_g:
+        raise SystemExit(json.dumps({"error": "split-row parity guard failed after the graph replays"}))
+    steps = reps * len(pools)
     tt = torch.tensor([e0.elapsed_time(e1)], device=dev)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item()) / steps
+    if world > 1:
+        dist.barrier()
+    del graph  # holds NCCL work: released before the process group
     alg = g.algorithmic_bytes()
     ref = None
     if world == 1 and not args.no_reference_kernel:
@@ -676,6 +716,7 @@ def split_config3(args, world, rank, local, steps: int | None = None) -> dict:
             "value": round(alg / (ms / 1e3) / 1e9, 1), "unit": "GB/s", "steps": steps,
             "l2": "16 rotating copies of the 9.5 MB page pool (152 MB > 126 MB L2)",
             "parallelism": f"page-range split, NCCL all-gather of 2048 (score, token) pairs per rank x{world}",
+            "timing": "CUDA graph of 16 steps (one per pool copy) replayed, CUDA events, max over ranks",
             "launches_per_call": 3, "clocks": clk}
 
 

@@ -36,7 +36,10 @@
 // Scorers never wait for selectors; selectors wait (bounded) only for rows
 // that scorers, all resident or scheduled as soon as any CTA retires, will
 // finish.  The row-claim and exit counters live in the workspace header and
-// are reset by the last selector to leave.
+// are reset by the last selector to leave.  A call that gave up a wait
+// (DSAI_STATUS_WAIT_TIMEOUT) may leave counters, histograms or the sentinel
+// incomplete: initialize the workspace again (dsai_workspace_init) before
+// its next use.
 //
 // Opt-in (DSAI_FUSED=1 in the environment).
 #include <cstdlib>

@@ -499,23 +499,21 @@ def small_shape_latency(steps: int, warmup: int, dev) -> dict:
     """Latency of small calls (the contest's workload sizes: B <= 31 rows of
     at most 91 pages), where per-call host work and kernel latency dominate:
     the drop-in kernel(...) called back to back (CUDA events over the calls,
-    and the host time to issue one call), and the same call replayed from a
-    CUDA graph (IndexerGraph; device time only)."""
-    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import IndexerGraph
+    and the host time to issue one call), the same call through the
+    library's graph cache (run(..., graph=True): one cached executable graph
+    per launch plan, pointers written into its nodes), and the call replayed
+    from a CUDA graph of fixed tensors (IndexerGraph; device time only)."""
+    from dsa_topk_indexer_fp8_h64_d128_topk2048_ps64_b200 import IndexerGraph, run
     shapes = {"config0 (B=2, L {1500, 4096}, 64 pages)": W.config_inputs(0, device=dev),
               "B=14, L 1924..5824, 91 pages": W.make_inputs(list(range(5824 - 13 * 300, 5825, 300)), max_pages=91,
                                                            seed=5, device=dev)}
     res = {}
-    for name, g in shapes.items():
-        out = g.out()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-        def call():
-            kernel(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out)
-
+    def timed(call):
         for _ in range(warmup + 20):
             call()
         torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         t0 = time.perf_counter()
         for _ in range(steps):
@@ -523,21 +521,19 @@ def small_shape_latency(steps: int, warmup: int, dev) -> dict:
         t1 = time.perf_counter()
         e1.record()
         torch.cuda.synchronize()
-        eager = e0.elapsed_time(e1) / steps * 1e3
-        host = (t1 - t0) / steps * 1e6
+        return e0.elapsed_time(e1) / steps * 1e3, (t1 - t0) / steps * 1e6
+
+    for name, g in shapes.items():
+        out = g.out()
+        eager, host = timed(lambda: kernel(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out))
+        cached, chost = timed(lambda: run(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out, graph=True))
         gr = IndexerGraph(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out)
-        for _ in range(warmup + 20):
-            gr.replay()
-        torch.cuda.synchronize()
-        e0.record()
-        for _ in range(steps):
-            gr.replay()
-        e1.record()
-        torch.cuda.synchronize()
+        replay, _ = timed(gr.replay)
         res[name] = {"eager_us_per_call": round(eager, 2), "host_us_per_call": round(host, 2),
-                     "graph_replay_us_per_call": round(e0.elapsed_time(e1) / steps * 1e3, 2)}
+                     "graph_cache_us_per_call": round(cached, 2), "graph_cache_host_us_per_call": round(chost, 2),
+                     "graph_replay_us_per_call": round(replay, 2)}
         del gr
-    res["timing"] = (f"{steps} back-to-back calls, CUDA events; host = time to issue one kernel(...) call "
+    res["timing"] = (f"{steps} back-to-back calls, CUDA events; host = time to issue one call "
                      "(perf_counter, no synchronisation inside)")
     return res
 

@@ -30,6 +30,7 @@ ATTN_HEADS = 16
 ATTN_CKV_DIM = 512
 ATTN_KPE_DIM = 64
 FLAG_SCORE_ALL_ROWS = 0x1
+FLAG_GRAPH = 0x2
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 E_INVALID = -1      # DSAI_E_* return codes
@@ -41,7 +42,7 @@ EXPORTED_SYMBOLS = (
     "dsai_workspace_size", "dsai_workspace_init", "dsai_run", "dsai_run_pairs",
     "dsai_merge_pairs", "dsai_read_status", "dsai_last_error", "dsai_version",
     "dsai_run_noalloc", "dsai_noalloc_read_status", "dsai_selftest_wait_timeout", "dsai_write_k",
-    "dsai_sparse_attn_workspace_size", "dsai_sparse_attn",
+    "dsai_sparse_attn_workspace_size", "dsai_sparse_attn", "dsai_graph_cache_entries",
 )
 
 
@@ -127,6 +128,8 @@ def load_library(path: Path | None = None) -> ctypes.CDLL:
         lib.dsai_last_error.restype = ctypes.c_char_p
         lib.dsai_version.argtypes = []
         lib.dsai_version.restype = ctypes.c_char_p
+        lib.dsai_graph_cache_entries.argtypes = []
+        lib.dsai_graph_cache_entries.restype = ctypes.c_int
         _lib = lib
         return lib
 

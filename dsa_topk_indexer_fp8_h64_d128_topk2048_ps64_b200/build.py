@@ -16,8 +16,8 @@ PKG_DIR = Path(__file__).resolve().parent
 REPO = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_PATH = PKG_DIR / "libdsai.so"
-SOURCES = ["score.cu", "score_mq.cu", "fused.cu", "select.cu", "api.cu", "noalloc.cu", "writer.cu", "attn.cu"]
-HEADERS = ["common.cuh", "sm100.cuh", "launch.h", "tiles.cuh", "radix.cuh"]
+SOURCES = ["score.cu", "score_mq.cu", "fused.cu", "select.cu", "api.cu", "graph.cu", "noalloc.cu", "writer.cu", "attn.cu"]
+HEADERS = ["common.cuh", "sm100.cuh", "launch.h", "tiles.cuh", "radix.cuh", "graph.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

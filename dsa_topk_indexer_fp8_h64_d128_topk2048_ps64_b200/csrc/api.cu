@@ -18,6 +18,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "graph.h"
 #include "launch.h"
 
 namespace {
@@ -297,6 +298,40 @@ int run_scoring(const dsai_args* a, float* logits, uint32_t* hist, int* status, 
   return DSAI_OK;
 }
 
+// Whether `s` is capturing into a graph (a query that fails counts as
+// capturing: the launches then go directly onto the stream).
+bool stream_capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &st) != cudaSuccess) {
+    cudaGetLastError();  // not the caller's error: clear it
+    return true;
+  }
+  return st != cudaStreamCaptureStatusNone;
+}
+
+// Runs `plan` (a call's launches).  With `graph`, the launches are recorded
+// and replayed from the cached executable graph of their plan; a plan that
+// cannot be cached runs directly.
+template <class F>
+int run_launches(bool graph, cudaStream_t stream, F&& plan) {
+  if (graph) {
+    dsai::LaunchRecorder rec;
+    int rc;
+    {
+      dsai::RecordScope scope(&rec);
+      rc = plan();
+    }
+    if (rc == DSAI_OK) {
+      const cudaError_t e = dsai::replay_recorded(rec, stream);
+      if (e == cudaSuccess) return DSAI_OK;
+      if (e != cudaErrorNotSupported) return cuda_fail(e, "CUDA graph replay");
+    } else if (!rec.overflow) {
+      return rc;
+    }
+  }
+  return plan();
+}
+
 }  // namespace
 
 namespace dsai {
@@ -330,6 +365,7 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
   int* status = static_cast<int*>(workspace);
   const bool score_all = (a->flags & DSAI_FLAG_SCORE_ALL_ROWS) != 0;
   const bool all_short = static_cast<long long>(a->max_pages) * dsai::kPage <= dsai::kTopK;
+  const bool graph = (a->flags & DSAI_FLAG_GRAPH) != 0 && !a->ev_after_score && !stream_capturing(stream);
 
   if (all_short && !score_all) {
     // No row can exceed the top-K: the answer does not depend on scores.
@@ -337,10 +373,12 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
       cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
       if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
     }
-    cudaError_t e = dsai::launch_short_rows(a->seq_lens, a->block_table, a->rows, a->max_pages,
-                                            a->topk_indices, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "short-rows kernel launch");
-    return DSAI_OK;
+    return run_launches(graph, stream, [&]() -> int {
+      cudaError_t e = dsai::launch_short_rows(a->seq_lens, a->block_table, a->rows, a->max_pages,
+                                              a->topk_indices, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "short-rows kernel launch");
+      return DSAI_OK;
+    });
   }
   rc = check_scoring_args(a);
   if (rc) return rc;
@@ -396,31 +434,35 @@ int dsai_run(const dsai_args* a, void* workspace, size_t workspace_bytes, void* 
     return DSAI_OK;
   }
   if (!a->logits_out) forget_sentinel(workspace);
-  rc = run_scoring(a, logits, hist, status, score_all, dev.sms, stream);
-  if (rc) return rc;
-  if (a->ev_after_score) {
-    cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
-  }
-  dsai::SelectLaunch sp;
-  sp.logits = logits;
-  sp.ld = a->max_pages * dsai::kPage;
-  sp.hist = hist;
-  sp.cand = ws_cand(workspace, a->rows);
-  sp.seq_lens = a->seq_lens;
-  sp.block_table = a->block_table;
-  sp.rows = a->rows;
-  sp.max_pages = a->max_pages;
-  sp.status = status;
-  sp.out_ids = a->topk_indices;
-  sp.out_scores = nullptr;
-  sp.out_tokens = nullptr;
-  sp.token_offset = 0;
-  sp.sms = dev.sms;
-  cudaError_t e = dsai::launch_select(sp, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
-  return DSAI_OK;
+  return run_launches(graph, stream, [&]() -> int {
+    int rc2 = run_scoring(a, logits, hist, status, score_all, dev.sms, stream);
+    if (rc2) return rc2;
+    if (a->ev_after_score) {
+      cudaError_t e = cudaEventRecord(static_cast<cudaEvent_t>(a->ev_after_score), stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    }
+    dsai::SelectLaunch sp;
+    sp.logits = logits;
+    sp.ld = a->max_pages * dsai::kPage;
+    sp.hist = hist;
+    sp.cand = ws_cand(workspace, a->rows);
+    sp.seq_lens = a->seq_lens;
+    sp.block_table = a->block_table;
+    sp.rows = a->rows;
+    sp.max_pages = a->max_pages;
+    sp.status = status;
+    sp.out_ids = a->topk_indices;
+    sp.out_scores = nullptr;
+    sp.out_tokens = nullptr;
+    sp.token_offset = 0;
+    sp.sms = dev.sms;
+    cudaError_t e = dsai::launch_select(sp, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "select kernel launch");
+    return DSAI_OK;
+  });
 }
+
+int dsai_graph_cache_entries(void) { return dsai::graph_cache_entries(); }
 
 int dsai_run_pairs(const dsai_args* a, int32_t token_offset, float* out_scores, int32_t* out_tokens,
                    void* workspace, size_t workspace_bytes, void* stream_) {

@@ -32,6 +32,7 @@
 //               can never leave the others waiting).
 // Rows with L <= 2048 are skipped (their output does not depend on scores).
 #include "common.cuh"
+#include "graph.h"
 #include "launch.h"
 #include "sm100.cuh"
 #include "tiles.cuh"
@@ -441,7 +442,7 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, score_kernel, tmap_q, tmap_k, tmap_s, p);
+  return launch_kernel(cfg, score_kernel, tmap_q, tmap_k, tmap_s, p);
 }
 
 }  // namespace dsai

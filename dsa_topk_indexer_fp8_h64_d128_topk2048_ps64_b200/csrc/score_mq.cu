@@ -34,6 +34,7 @@
 //               logit is stored and reduced into its row's histogram (one
 //               reduction per token), with the row's own length.
 #include "common.cuh"
+#include "graph.h"
 #include "launch.h"
 #include "sm100.cuh"
 #include "tiles.cuh"
@@ -514,7 +515,7 @@ cudaError_t launch_mq(const ScoreLaunch& lp, const CUtensorMap& tq, const CUtens
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, score_mq_kernel<R>, tq, tk, ts, p);
+  return launch_kernel(cfg, score_mq_kernel<R>, tq, tk, ts, p);
 }
 
 }  // namespace

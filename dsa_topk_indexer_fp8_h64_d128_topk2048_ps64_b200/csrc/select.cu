@@ -60,6 +60,7 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "graph.h"
 #include "launch.h"
 #include "radix.cuh"
 #include "sm100.cuh"
@@ -1442,8 +1443,8 @@ cudaError_t launch_select_split(const SelectLaunch& p, long long chunks_per_row,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const int cpr = static_cast<int>(chunks_per_row);
-  if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_split_kernel<true>, p, cpr);
-  return cudaLaunchKernelEx(&cfg, select_split_kernel<false>, p, cpr);
+  if (p.out_ids) return launch_kernel(cfg, select_split_kernel<true>, p, cpr);
+  return launch_kernel(cfg, select_split_kernel<false>, p, cpr);
 }
 
 cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
@@ -1480,18 +1481,21 @@ cudaError_t launch_select(const SelectLaunch& p, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = sh.cluster > 1 ? 2 : 1;
   if (sh.threads == kWThreads) {
-    if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_wide_kernel<true>, p);
-    return cudaLaunchKernelEx(&cfg, select_wide_kernel<false>, p);
+    if (p.out_ids) return launch_kernel(cfg, select_wide_kernel<true>, p);
+    return launch_kernel(cfg, select_wide_kernel<false>, p);
   }
-  if (p.out_ids) return cudaLaunchKernelEx(&cfg, select_rows_kernel<true, 256>, p);
-  return cudaLaunchKernelEx(&cfg, select_rows_kernel<false, 256>, p);
+  if (p.out_ids) return launch_kernel(cfg, select_rows_kernel<true, 256>, p);
+  return launch_kernel(cfg, select_rows_kernel<false, 256>, p);
 }
 
 cudaError_t launch_short_rows(const int32_t* seq_lens, const int32_t* block_table, int rows,
                               int max_pages, int32_t* out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  short_rows_kernel<<<rows, 128, 0, stream>>>(seq_lens, block_table, max_pages, out);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows));
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  return launch_kernel(cfg, short_rows_kernel, seq_lens, block_table, max_pages, out);
 }
 
 cudaError_t launch_wait_selftest(int* status, unsigned long long timeout_ns, cudaStream_t stream) {

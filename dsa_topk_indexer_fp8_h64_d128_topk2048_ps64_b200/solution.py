@@ -14,6 +14,7 @@ no host synchronisation.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -27,6 +28,11 @@ _FP8 = getattr(torch, "float8_e4m3fn", None)
 # and the raw stream handle are read without building torch.cuda objects.
 _current_device = torch._C._cuda_getDevice
 _current_raw_stream = torch._C._cuda_getCurrentRawStream
+# DSAI_GRAPH=1 in the environment (read once) makes kernel() launch through
+# the library's graph cache, as run(..., graph=True) does.  Off by default:
+# replays cut the host work per call but give up the programmatic overlap of
+# one call's first kernel with the previous call's last.
+_KERNEL_GRAPH = os.environ.get("DSAI_GRAPH", "0") == "1"
 
 
 def _call_on(dev_index: int, fn, *args) -> int:
@@ -81,7 +87,7 @@ def _args(q, k, w, seq_lens, block_table, out, logits_out, flags: int, rows_per_
 def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices,
         logits_out: torch.Tensor | None = None, score_all_rows: bool = False,
         event_after_score: torch.cuda.Event | None = None, workspace: "_lib.Workspace | None" = None,
-        rows_per_seq: int = 1):
+        rows_per_seq: int = 1, graph: bool = False):
     """The indexer with optional extras: ``logits_out`` ([B, max_pages*64]
     fp32) receives the scored logits (entries at t >= seq_len are left
     untouched; rows with seq_len <= 2048 are scored only with
@@ -91,7 +97,12 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
     (multi-query decode, next-n / MTP, causal prefill rows) that agree on
     ``block_table`` over every page each of them reaches: each group's K
     pages are then read once, through the block-table row of its longest
-    row.  The results are those of independent rows."""
+    row.  The results are those of independent rows.  ``graph`` launches the
+    call's kernels as one CUDA graph from the library's cache of executable
+    graphs (one per device, stream and launch plan; the call's pointers are
+    written into the cached graph's kernel nodes, nothing is re-captured):
+    the reference's replay of every call from a graph cache
+    (solution/python/kernel.cu:1101-1199)."""
     _check_int32(block_table, "block_table")
     _check_int32(seq_lens, "seq_lens")
     _check_int32(topk_indices, "topk_indices")
@@ -118,7 +129,8 @@ def run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_ind
     ws_ptr, ws_bytes = ws.get(rows, max_pages, stream)
     a = _args(q_index_fp8 if needs_scoring else None, k_index_cache_fp8 if needs_scoring else None,
               weights if needs_scoring else None, seq_lens, block_table, topk_indices, logits_out,
-              _lib.FLAG_SCORE_ALL_ROWS if score_all_rows else 0, rows_per_seq)
+              (_lib.FLAG_SCORE_ALL_ROWS if score_all_rows else 0) | (_lib.FLAG_GRAPH if graph else 0),
+              rows_per_seq)
     if needs_scoring:
         a.num_pages = k_index_cache_fp8.numel() // _lib.PAGE_BYTES
     if event_after_score is not None:
@@ -130,7 +142,7 @@ def kernel(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_
     """Drop-in for the reference's ``solution.py::kernel``: writes the top-2048
     physical slot ids of every row into ``topk_indices`` ([B, 2048] int32,
     -1 padded) and returns None."""
-    run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices)
+    run(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, topk_indices, graph=_KERNEL_GRAPH)
 
 
 def run_pairs(q_index_fp8, k_index_cache_fp8, weights, seq_lens, block_table, token_offset: int,

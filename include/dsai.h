@@ -69,6 +69,16 @@ extern "C" {
 
 /* Flags for dsai_args.flags. */
 #define DSAI_FLAG_SCORE_ALL_ROWS 0x1 /* also score rows with seq_len <= 2048 (debug logits) */
+/* Launch the call's kernels as one cached CUDA graph: the executable graph is
+ * kept per (device, stream, launch plan = kernels, grids, blocks, shared
+ * memory), captured on the first call of a plan, and later calls write their
+ * pointers and sizes into its kernel nodes and launch it (no re-capture).
+ * The reference's host entry point replays every call from such a cache
+ * (solution/python/kernel.cu:1101-1199, :1389-1478).  Ignored (the kernels
+ * are launched directly) when ev_after_score is set, when the caller's
+ * stream is itself capturing, for the opt-in fused launch, and once 64 plans
+ * are cached. */
+#define DSAI_FLAG_GRAPH 0x2
 
 typedef struct dsai_args {
   const void* q;             /* [rows, 64, 128] float8_e4m3fn                         */
@@ -113,6 +123,12 @@ DSAI_API int dsai_workspace_init(void* workspace, size_t workspace_bytes, void* 
  * TVM-FFI export `kernel` (solution/cuda/kernel.cu:430-507). */
 DSAI_API int dsai_run(const dsai_args* args, void* workspace, size_t workspace_bytes,
              void* stream);
+
+/* Executable graphs held by the DSAI_FLAG_GRAPH cache (all devices and
+ * streams).  The reference keeps its cache internal
+ * (solution/python/kernel.cu:1133-1199); exported here so that callers and
+ * tests can see whether calls replay a cached plan or capture new ones. */
+DSAI_API int dsai_graph_cache_entries(void);
 
 /* Per-row top-2048 as (fp32 score, token index + token_offset) pairs, for a
  * caller that merges several partial rows (a long row split by page range

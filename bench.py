@@ -72,10 +72,10 @@ FALLBACK_HBM_GBS = 6650.0
 # reports it only while the sources still hash the same; otherwise it is
 # null and the old capture is shown as traffic_last_profiled.
 SCORE_TRAFFIC = {
-    1: {"bytes": 156_326_656 + 5_183_488, "kernel": "score_kernel",
-        "src_sha256": "d68907fb8cba24ffb545aa4cadda61aab1e7aa97c8ba6973a1b7d2ea6fe5f7e2"},
-    4: {"bytes": 156_798_464 + 8_856_832, "kernel": "score_mq_kernel<4>",
-        "src_sha256": "485f0dec96c7cbd5e1e23e69eeb41448adb0126de3960579c144803ccb97a419"},
+    1: {"bytes": 156_326_656 + 5_213_440, "kernel": "score_kernel",
+        "src_sha256": "e9dfb7619afcaa35a2fccbfc091f489e75ebb59df03bc2a0a6b630c5020243e0"},
+    4: {"bytes": 156_744_448 + 6_459_136, "kernel": "score_mq_kernel<4>",
+        "src_sha256": "0dab5fb9f9b421e936b27d330bd289e0645added1da744c932a7cdfad5189a24"},
 }
 N_SETS = 3
 

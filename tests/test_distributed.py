@@ -80,9 +80,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("seq_len", [9000, 1500])
-def test_split_row_on_two_gloo_ranks_matches_direct(oracle_mod, seq_len):
-    world = 2
+@pytest.mark.parametrize("seq_len,world", [(9000, 2), (1500, 2), (9000, 4)])
+def test_split_row_on_gloo_ranks_matches_direct(oracle_mod, seq_len, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -112,7 +111,7 @@ def _gather_worker(rank, world, port, result_q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        counts = [3, 2]
+        counts = [3, 2, 0, 1][:world]
         local = torch.arange(counts[rank] * TOPK, dtype=torch.int32).view(counts[rank], TOPK) + 100000 * rank
         buf = torch.empty((world, max(counts), TOPK), dtype=torch.int32)
         got = D.gather_rows(local, counts, buf=buf)
@@ -122,10 +121,10 @@ def _gather_worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
-def test_gather_rows_on_two_gloo_ranks():
-    """Rows sharded unevenly (3 and 2 rows): every rank gets all 5 rows in
-    rank order."""
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_gather_rows_on_gloo_ranks(world):
+    """Rows sharded unevenly (3, 2, 0 and 1 rows): every rank gets all rows
+    in rank order."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -139,7 +138,8 @@ def test_gather_rows_on_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    exp = np.concatenate([np.arange(3 * TOPK, dtype=np.int32).reshape(3, TOPK),
-                          np.arange(2 * TOPK, dtype=np.int32).reshape(2, TOPK) + 100000])
+    counts = [3, 2, 0, 1][:world]
+    exp = np.concatenate([np.arange(c * TOPK, dtype=np.int32).reshape(c, TOPK) + 100000 * g
+                          for g, c in enumerate(counts)])
     for r in range(world):
         assert np.array_equal(results[r][0], exp) and np.array_equal(results[r][1], exp)

@@ -387,9 +387,7 @@ def dist_setup(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1 and args.impl == "ours":
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        # bound to this rank's GPU: barriers and collectives use it without guessing
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
     return world, rank, local
 
 

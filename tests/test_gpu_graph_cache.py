@@ -18,29 +18,37 @@ DEV = torch.device("cuda", 0)
 def _fresh(inp: W.Inputs) -> W.Inputs:
     """The same contents in newly allocated tensors."""
     return W.Inputs(inp.q.clone(), inp.k_cache.clone(), inp.weights.clone(), inp.seq_lens.clone(),
-                    inp.block_table.clone())
+                    inp.block_table.clone(), rows_per_seq=inp.rows_per_seq)
 
 
-def _check(oracle_mod, inp: W.Inputs, got: np.ndarray, lg=None):
+def _check(oracle_mod, inp: W.Inputs, got: np.ndarray, lg=None, rows=None):
     d = inp.numpy()
     if lg is None:
         _, lg = oracle_mod.run(d["q"], d["k_cache"], d["weights"], d["seq_lens"], d["block_table"])
-    for b in range(inp.rows):
+    for b in (range(inp.rows) if rows is None else rows):
         L = int(min(max(d["seq_lens"][b], 0), inp.max_pages * 64))
         oracle_mod.check_row(got[b], lg[b], d["block_table"][b], L)
 
 
+# (inputs, rows checked against the oracle: None = all)
 CASES = {
-    "scored": lambda: W.make_inputs([1500, 4096, 9001, 2049, 30000, 0], max_pages=480, pool_pages=1500, seed=41),
-    "short": lambda: W.make_inputs([1, 63, 64, 65, 2048, 0, 700], max_pages=32, seed=42),
-    "many_rows": lambda: W.config_inputs(1, seed=43, rows=48),
+    "scored": (lambda: W.make_inputs([1500, 4096, 9001, 2049, 30000, 0], max_pages=480, pool_pages=1500, seed=41), None),
+    "short": (lambda: W.make_inputs([1, 63, 64, 65, 2048, 0, 700], max_pages=32, seed=42), None),
+    "many_rows": (lambda: W.config_inputs(1, seed=43, rows=48), None),
+    # more rows than one scoring launch takes (1024): three scoring launches and
+    # the selection in one recorded plan
+    "launch_chunks": (lambda: W.make_inputs(np.where(np.arange(2100) % 97 == 0, 3000, 2100).tolist(), seed=47),
+                      [0, 1, 97, 1023, 1024, 1025, 2047, 2048, 2049, 2099]),
+    # groups of four query rows sharing K pages (the grouped scorer)
+    "groups": (lambda: W.config_inputs(4, seed=48, rows=16), None),
 }
 
 
 @pytest.mark.parametrize("case", sorted(CASES))
 def test_graph_calls_with_fresh_tensors_match_oracle(oracle_mod, case):
     lib = _lib.load_library()
-    host = CASES[case]()
+    make, check_rows = CASES[case]
+    host = make()
     base = host.to(DEV)
     d = host.numpy()
     _, lg = oracle_mod.run(d["q"], d["k_cache"], d["weights"], d["seq_lens"], d["block_table"])
@@ -49,9 +57,9 @@ def test_graph_calls_with_fresh_tensors_match_oracle(oracle_mod, case):
         g = _fresh(base)
         out = g.out()
         out.fill_(-7)
-        run(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out, graph=True)
+        run(g.q, g.k_cache, g.weights, g.seq_lens, g.block_table, out, graph=True, rows_per_seq=g.rows_per_seq)
         torch.cuda.synchronize()
-        _check(oracle_mod, host, out.cpu().numpy(), lg)
+        _check(oracle_mod, host, out.cpu().numpy(), lg, check_rows)
         # one plan for all four calls: captured by the first, replayed after
         assert lib.dsai_graph_cache_entries() == before + 1
     assert read_status(DEV) == 0

@@ -170,7 +170,13 @@ cudaError_t replay_recorded(const LaunchRecorder& r, cudaStream_t stream) {
   if (!ent) {
     if (static_cast<int>(g_entries.size()) >= kGraphCacheMax) return cudaErrorNotSupported;
     ent = capture(dev, stream, r, &e);
-    if (!ent) return e;
+    if (!ent) {
+      // A plan that cannot be captured here (for instance another capture in
+      // global mode on this device) is launched directly; a real launch
+      // error shows up there.
+      cudaGetLastError();
+      return cudaErrorNotSupported;
+    }
     g_entries.push_back(ent);
     return cudaGraphLaunch(ent->exec, stream);  // captured with this call's arguments
   }

@@ -114,8 +114,8 @@ cudaError_t launch_kernel(const cudaLaunchConfig_t& cfg, void (*k)(KArgs...), Ar
 
 // Launches the recorded kernels on `stream` as one cached executable graph
 // (see above).  Returns cudaErrorNotSupported, having launched nothing, when
-// the plan cannot be cached (the cache is full); the caller then launches
-// directly.
+// the plan cannot be cached (the cache is full, or the capture failed); the
+// caller then launches directly.
 cudaError_t replay_recorded(const LaunchRecorder& r, cudaStream_t stream);
 
 // Number of executable graphs in the cache (all devices and streams).

@@ -44,6 +44,11 @@ constexpr uint64_t kWaitTimeoutNs = 1000000000ull;  // 1 s bound on any on-chip 
 
 // Workspace header: status word at offset 0, data from kWsHeader on.
 constexpr size_t kWsHeader = 256;
+// Control words in the header (int offsets; zero between launches): the
+// scorer's next chunk to deal out and its CTAs finished.  (The opt-in fused
+// launch keeps its own at ints 16 and 48.)
+constexpr int kHdrScoreNext = 24;
+constexpr int kHdrScoreDone = 32;
 
 __device__ __forceinline__ void report(int* status, int bits) {
   if (status) atomicOr(status, bits);

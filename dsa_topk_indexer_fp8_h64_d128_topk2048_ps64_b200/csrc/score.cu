@@ -9,9 +9,15 @@
 //
 // Work decomposition.  A row of L tokens is cut into ceil(L/128) tiles of two
 // 64-token pages (M = 128 of one UMMA).  All tiles of all scored rows form
-// one flat sequence; CTA c of a persistent grid takes the contiguous slice
-// [c*T/G, (c+1)*T/G), so every CTA moves the same number of K bytes and
-// crosses at most a few row boundaries (Q is reloaded only there).
+// one flat sequence of T tiles.  Its first part (T - D tiles) is cut into
+// contiguous static slices, one per CTA of the persistent grid; its last D
+// tiles are dealt out in chunks of `chunk` tiles that CTAs claim with one
+// atomic on a counter in the workspace header as they run out of work, so
+// CTAs that start late (their SM still held by the previous kernel) or run
+// slow take fewer tiles and the grid ends together.  The producer hands each
+// chunk's tile range to the MMA and epilogue warps through a small shared-
+// memory ring; the last CTA to finish resets the counters for the next
+// launch.  Q is reloaded only at row changes.
 //
 // Two CTAs per SM (two independent pipelines per SM overlap each other's
 // latencies), 6 warps each, warp-specialised:
@@ -19,7 +25,7 @@
 //               128-B swizzle) into a 5-stage K ring, its 64 scales into a
 //               16-slot scale ring, and the row's Q (8 KB) into a 2-slot ring.
 //               The 32 lanes resolve the pages of 32 tiles at once, one batch
-//               ahead, so the block-table pointer chase never stalls issue.
+//               ahead within a chunk.
 //   warp 1      MMA issuer (one lane): 4 x tcgen05.mma kind::f8f6f4
 //               M128 N64 K32 per tile into one of 4 TMEM accumulators.  A K
 //               stage is released as soon as its MMAs complete.
@@ -31,6 +37,8 @@
 //               group synchronisation beyond the warp, so a timed-out warp
 //               can never leave the others waiting).
 // Rows with L <= 2048 are skipped (their output does not depend on scores).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "graph.h"
 #include "launch.h"
@@ -65,12 +73,26 @@ struct ScoreParams {
   int ld;
   int row_base;
   int score_all;
+  int dyn_pct;        // percent of the tile sequence dealt out in chunks (0: static slices only) ...
+  int dyn_per_cta;    // ... but at most this many tiles per CTA of the grid
+  int chunk;          // tiles per claimed chunk
 };
+
+constexpr int kChunkSlots = 4;  // chunk ranges in flight from the producer to the consumers
+constexpr int kDynPercent = 25;  // default share of the tile sequence dealt out in chunks,
+constexpr int kDynPerCta = 8;    // capped at this many tiles per CTA
+constexpr int kDynChunk = 4;     // default tiles per chunk
+
+int env_int_or(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return (v && *v) ? atoi(v) : dflt;
+}
 
 struct ScoreSmem {
   uint8_t k[kStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
   uint8_t q[2][kQBytes];                // SW128 K-major, N = 64 heads
   float scale[kScaleSlots][kTileTok];
+  int2 chunk[kChunkSlots];              // tile range [x, y) of a chunk; x < 0: no more work
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t sfull[kScaleSlots];
@@ -79,6 +101,8 @@ struct ScoreSmem {
   uint64_t qempty[2];
   uint64_t tfull[kAccs];
   uint64_t tempty[kAccs];
+  uint64_t cfull[kChunkSlots];
+  uint64_t cempty[kChunkSlots];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -140,6 +164,12 @@ __device__ __forceinline__ TileRef resolve_tile(const ScoreSmem& s, const ScoreP
   return r;
 }
 
+// Position in the ring of chunk ranges (slot and phase parity).
+struct ChunkRing {
+  int slot = 0;
+  uint32_t phase = 0;
+};
+
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     score_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  const __grid_constant__ CUtensorMap tmap_k,
@@ -170,6 +200,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], kEpiThreads / 32);
     }
+    for (int i = 0; i < kChunkSlots; ++i) {
+      mbar_init(&s.cfull[i], 1);
+      mbar_init(&s.cempty[i], 1 + kEpiThreads / 32);  // the MMA issuer + the epilogue warps
+    }
     mbar_init(&s.drain, 1);
     s.abort = 0;
     fence_mbar_init();
@@ -192,43 +226,70 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   const int* rs = s.row_start;
   const int T = rs[p.rows];
-  const int t0 = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / gridDim.x);
-  const int t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / gridDim.x);
+  // Tiles dealt out in chunks: enough to absorb CTAs that start late or run
+  // slow (a few tiles each), not a share that grows with the sequence.
+  const int D = static_cast<int>(min(static_cast<long long>(T) * min(100, max(0, p.dyn_pct)) / 100,
+                                     static_cast<long long>(gridDim.x) * max(0, p.dyn_per_cta)));
+  const int TS = T - D;                           // tiles in static slices
+  const int C = max(1, p.chunk);
+  const int nchunks = (D + C - 1) / C;
+  const int t0 = static_cast<int>((static_cast<long long>(TS) * blockIdx.x) / gridDim.x);
+  const int t1 = static_cast<int>((static_cast<long long>(TS) * (blockIdx.x + 1)) / gridDim.x);
+  int* const claim_ctr = p.status + kHdrScoreNext;
 
-  if (t0 < t1) {
-    if (warp == 0) {
-      // ------------------------------------------------------------ producer
-      const uint64_t pol_k = l2_policy_evict_first();
-      const uint64_t pol_q = l2_policy_evict_last();
-      int stage = 0, sslot = 0, qs = 1, cur_row = -1;
-      uint32_t phase = 0, sphase = 0;
-      uint32_t qe_par[2] = {0u, 0u};
-      int q_uses[2] = {0, 0};
-      int k_fills = 0, s_fills = 0;
-      bool ok = true;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol_k = l2_policy_evict_first();
+    const uint64_t pol_q = l2_policy_evict_last();
+    int stage = 0, sslot = 0, qs = 1, cur_row = -1;
+    uint32_t phase = 0, sphase = 0;
+    uint32_t qe_par[2] = {0u, 0u};
+    int q_uses[2] = {0, 0};
+    int k_fills = 0, s_fills = 0;
+    ChunkRing ring;
+    bool ok = true;
+    bool claims_left = nchunks > 0;
+    int cb = t0, ce = t1;  // the static slice first
+    while (ok) {
+      // Publish [cb, ce) (cb < 0: no more work) to the MMA issuer and the epilogue.
+      int good = 1;
+      if (lane == 0) {
+        if (!mbar_wait(&s.cempty[ring.slot], ring.phase ^ 1u, &s.abort, kWaitTimeoutNs)) {
+          good = 0;
+          fail(s, p.status);
+        } else {
+          s.chunk[ring.slot] = make_int2(cb, ce);
+          mbar_arrive(&s.cfull[ring.slot]);
+        }
+      }
+      if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+      good = __shfl_sync(0xffffffffu, good, 0);
+      if (!good || cb < 0) break;
+
       TileRef nxt = {0, 0, 0, 0};
-      if (t0 + lane < t1) nxt = resolve_tile(s, p, t0 + lane);
-      for (int tb = t0; tb < t1 && ok; tb += 32) {
+      if (cb + lane < ce) nxt = resolve_tile(s, p, cb + lane);
+      for (int tb = cb; tb < ce && ok; tb += 32) {
         const TileRef cur = nxt;
-        // Resolve the next batch now; its loads overlap this batch's issue.
-        if (tb + 32 + lane < t1) nxt = resolve_tile(s, p, tb + 32 + lane);
-        if (tb + lane < t1 &&
+        // Resolve the chunk's next batch now; its loads overlap this batch's issue.
+        if (tb + 32 + lane < ce) nxt = resolve_tile(s, p, tb + 32 + lane);
+        if (tb + lane < ce &&
             (static_cast<unsigned>(cur.pg0) >= static_cast<unsigned>(p.num_pages) ||
              (cur.two && static_cast<unsigned>(cur.pg1) >= static_cast<unsigned>(p.num_pages))))
           report(p.status, DSAI_STATUS_BAD_PAGE);  // TMA zero-fills out-of-range pages
-        const int n = min(32, t1 - tb);
+        const int n = min(32, ce - tb);
         for (int i = 0; i < n; ++i) {
           const int r = __shfl_sync(0xffffffffu, cur.row, i);
           const int a = __shfl_sync(0xffffffffu, cur.pg0, i);
           const int b = __shfl_sync(0xffffffffu, cur.pg1, i);
           const int tw = __shfl_sync(0xffffffffu, cur.two, i);
-          int good = 1;
+          int g = 1;
           if (lane == 0) {
             if (r != cur_row) {
               cur_row = r;
               qs ^= 1;
+              // The slot is free once the MMAs of its last row completed.
               if (!mbar_wait(&s.qempty[qs], qe_par[qs] ^ 1u, &s.abort, kWaitTimeoutNs)) {
-                good = 0;
+                g = 0;
               } else {
                 qe_par[qs] ^= 1u;
                 ++q_uses[qs];
@@ -236,9 +297,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 tma_load_2d(s.q[qs], &tmap_q, &s.qfull[qs], 0, (p.row_base + r) * kHeads, pol_q);
               }
             }
-            if (good && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs)) good = 0;
-            if (good && !mbar_wait(&s.sempty[sslot], sphase ^ 1u, &s.abort, kWaitTimeoutNs)) good = 0;
-            if (good) {
+            if (g && !mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, kWaitTimeoutNs)) g = 0;
+            if (g && !mbar_wait(&s.sempty[sslot], sphase ^ 1u, &s.abort, kWaitTimeoutNs)) g = 0;
+            if (g) {
               mbar_arrive_expect_tx(&s.full[stage], tw ? 2 * kPageKBytes : kPageKBytes);
               mbar_arrive_expect_tx(&s.sfull[sslot], tw ? 2 * kScaleTx : kScaleTx);
               tma_load_3d(s.k[stage], &tmap_k, &s.full[stage], 0, 0, a, pol_k);
@@ -255,47 +316,73 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               fail(s, p.status);
             }
           }
-          good = __shfl_sync(0xffffffffu, good, 0);
-          if (!good) { ok = false; break; }
+          g = __shfl_sync(0xffffffffu, g, 0);
+          if (!g) { ok = false; break; }
         }
       }
-      // Never leave with a TMA in flight: wait for the latest fill of every
-      // slot (each earlier fill of a slot was consumed, hence complete).
-      if (lane == 0) {
-        for (int i = 0; i < kStages && i < k_fills; ++i) {
-          const int last = k_fills - 1 - i;  // fill index of the i-th latest fill
-          if (!mbar_wait(&s.full[last % kStages], (last / kStages) & 1, nullptr, kWaitTimeoutNs))
-            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      // The next chunk, claimed only now that this one's tiles are all
+      // issued: the K ring still holds several tiles for the consumers, which
+      // covers the claim's latency, and no CTA sits on a chunk it has not
+      // started while others run dry at the end.
+      int nb = -1, ne = -1;
+      if (lane == 0 && ok && claims_left) {
+        const int k = atomicAdd(claim_ctr, 1);
+        if (k < nchunks) {
+          nb = TS + k * C;
+          ne = min(T, nb + C);
+        } else {
+          claims_left = false;
         }
-        for (int i = 0; i < kScaleSlots && i < s_fills; ++i) {
-          const int last = s_fills - 1 - i;
-          if (!mbar_wait(&s.sfull[last % kScaleSlots], (last / kScaleSlots) & 1, nullptr, kWaitTimeoutNs))
-            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
-        }
-        for (int i = 0; i < 2; ++i)
-          if (q_uses[i] > 0 && !mbar_wait(&s.qfull[i], (q_uses[i] - 1) & 1, nullptr, kWaitTimeoutNs))
-            report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
       }
-      __syncwarp();
-    } else if (warp == 1) {
-      // ------------------------------------------------------------ MMA issuer
-      if (lane == 0) {
-        constexpr uint32_t idesc = make_idesc_e4m3_f32(kTileTok, kHeads);
-        int stage = 0, acc = 0, qs = 1, cur_row = -1;
-        uint32_t phase = 0, aphase = 0;
-        uint32_t qf_par[2] = {0u, 0u};
+      cb = __shfl_sync(0xffffffffu, nb, 0);
+      ce = __shfl_sync(0xffffffffu, ne, 0);
+    }
+    // Never leave with a TMA in flight: wait for the latest fill of every
+    // slot (each earlier fill of a slot was consumed, hence complete).
+    if (lane == 0) {
+      for (int i = 0; i < kStages && i < k_fills; ++i) {
+        const int last = k_fills - 1 - i;  // fill index of the i-th latest fill
+        if (!mbar_wait(&s.full[last % kStages], (last / kStages) & 1, nullptr, kWaitTimeoutNs))
+          report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      }
+      for (int i = 0; i < kScaleSlots && i < s_fills; ++i) {
+        const int last = s_fills - 1 - i;
+        if (!mbar_wait(&s.sfull[last % kScaleSlots], (last / kScaleSlots) & 1, nullptr, kWaitTimeoutNs))
+          report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+      }
+      for (int i = 0; i < 2; ++i)
+        if (q_uses[i] > 0 && !mbar_wait(&s.qfull[i], (q_uses[i] - 1) & 1, nullptr, kWaitTimeoutNs))
+          report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_e4m3_f32(kTileTok, kHeads);
+      int stage = 0, acc = 0, qs = 1, cur_row = -1;
+      uint32_t phase = 0, aphase = 0;
+      uint32_t qf_par[2] = {0u, 0u};
+      ChunkRing ring;
+      bool ok = true;
+      while (ok) {
+        if (!mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+        const int2 ch = s.chunk[ring.slot];
+        mbar_arrive(&s.cempty[ring.slot]);
+        if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+        if (ch.x < 0) break;
+        if (ch.x >= ch.y) continue;
         Cursor c;
-        c.init(rs, p.rows, t0);
-        for (; c.t < t1; c.next(rs, t1)) {
+        c.init(rs, p.rows, ch.x);
+        for (; c.t < ch.y; c.next(rs, ch.y)) {
           if (c.row != cur_row) {
             if (cur_row >= 0) umma_commit(&s.qempty[qs]);  // previous row's Q free when done
             cur_row = c.row;
             qs ^= 1;
-            if (!mbar_wait(&s.qfull[qs], qf_par[qs], &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+            if (!mbar_wait(&s.qfull[qs], qf_par[qs], &s.abort, kWaitTimeoutNs)) { fail(s, p.status); ok = false; break; }
             qf_par[qs] ^= 1u;
           }
-          if (!mbar_wait(&s.full[stage], phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
-          if (!mbar_wait(&s.tempty[acc], aphase ^ 1u, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+          if (!mbar_wait(&s.full[stage], phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); ok = false; break; }
+          if (!mbar_wait(&s.tempty[acc], aphase ^ 1u, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); ok = false; break; }
           tc_fence_after();
           const uint64_t adesc = make_sw128_kmajor_desc(smem_u32(s.k[stage]));
           const uint64_t bdesc = make_sw128_kmajor_desc(smem_u32(s.q[qs]));
@@ -308,26 +395,43 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
           if (++acc == kAccs) { acc = 0; aphase ^= 1u; }
         }
-        // Every MMA issued by this thread has completed once this arrives.
-        umma_commit(&s.drain);
-        if (!mbar_wait(&s.drain, 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
       }
+      // Every MMA issued by this thread has completed once this arrives.
+      umma_commit(&s.drain);
+      if (!mbar_wait(&s.drain, 0, nullptr, kWaitTimeoutNs)) report(p.status, DSAI_STATUS_WAIT_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;              // TMEM lanes [32*quad, 32*quad+32)
+    const int tok = quad * 32 + lane;       // token of the tile owned by this thread
+    int acc = 0, sslot = 0, cur_row = -1, L = 0;
+    uint32_t aphase = 0, sphase = 0;
+    bool hist_row = false;
+    float w[kHeads];
+    float* out_row = nullptr;
+    uint32_t* hist_g = nullptr;
+    ChunkRing ring;
+    bool ok = true;
+    while (ok) {
+      // Waits are decided warp-wide: the warp runs warp-collective steps below.
+      if (!__all_sync(0xffffffffu, mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs))) {
+        fail(s, p.status);
+        break;
+      }
+      const int2 ch = s.chunk[ring.slot];
       __syncwarp();
-    } else {
-      // ------------------------------------------------------------ epilogue
-      const int quad = warp & 3;              // TMEM lanes [32*quad, 32*quad+32)
-      const int tok = quad * 32 + lane;       // token of the tile owned by this thread
-      int acc = 0, sslot = 0, cur_row = -1, L = 0;
-      uint32_t aphase = 0, sphase = 0;
-      bool hist_row = false;
-      float w[kHeads];
-      float* out_row = nullptr;
-      uint32_t* hist_g = nullptr;
+      if (lane == 0) mbar_arrive(&s.cempty[ring.slot]);
+      if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+      if (ch.x < 0) break;
+      if (ch.x >= ch.y) continue;
       Cursor c;
-      c.init(rs, p.rows, t0);
-      for (; c.t < t1; c.next(rs, t1)) {
+      c.init(rs, p.rows, ch.x);
+      for (; c.t < ch.y; c.next(rs, ch.y)) {
         if (c.row != cur_row) {
           cur_row = c.row;
+          // (Staging the weights in shared memory with the row's Q instead
+          // made the kernel ~1.8 us slower: the epilogue then waits for Q.)
           const float4* w4 = reinterpret_cast<const float4*>(p.weights + static_cast<size_t>(cur_row) * kHeads);
 #pragma unroll
           for (int i = 0; i < kHeads / 4; ++i) {
@@ -339,9 +443,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           out_row = p.logits + static_cast<size_t>(cur_row) * p.ld;
           hist_g = p.hist + static_cast<size_t>(cur_row) * kHistStride;
         }
-        // Waits are decided warp-wide: the warp runs warp-collective steps below.
         if (!__all_sync(0xffffffffu, mbar_wait(&s.tfull[acc], aphase, &s.abort, kWaitTimeoutNs))) {
           fail(s, p.status);
+          ok = false;
           break;
         }
         tc_fence_after();
@@ -356,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         if (lane == 0) mbar_arrive(&s.tempty[acc]);
         if (!__all_sync(0xffffffffu, mbar_wait(&s.sfull[sslot], sphase, &s.abort, kWaitTimeoutNs))) {
           fail(s, p.status);
+          ok = false;
           break;
         }
         const float sc = s.scale[sslot][tok];
@@ -401,6 +506,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     tc_fence_after();
     tmem_dealloc(s.tmem_base, kTmemCols);
   }
+  if (nchunks > 0 && tid == 0) {
+    // Every producer of this CTA has made its last claim (its claims returned
+    // before the barrier above).  The last CTA to get here resets both
+    // counters for the next launch on this workspace, which starts only
+    // after this grid has completed.
+    if (atomicAdd(p.status + kHdrScoreDone, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(claim_ctr, 0);
+      atomicExch(p.status + kHdrScoreDone, 0);
+    }
+  }
 }
 
 }  // namespace
@@ -432,6 +547,14 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   p.ld = lp.ld;
   p.row_base = lp.row_base;
   p.score_all = lp.score_all;
+  // The last part of the tile sequence is dealt out in chunks (both values
+  // can be overridden from the environment, read once, for measurements).
+  static const int dyn_pct = env_int_or("DSAI_SCORE_DYN", kDynPercent);
+  static const int dyn_per_cta = env_int_or("DSAI_SCORE_DYN_CTA", kDynPerCta);
+  static const int chunk = env_int_or("DSAI_SCORE_CHUNK", kDynChunk);
+  p.dyn_pct = dyn_pct;
+  p.dyn_per_cta = dyn_per_cta;
+  p.chunk = chunk > 0 ? chunk : 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(lp.grid * kCtasPerSm);
   cfg.blockDim = dim3(kThreads);

@@ -16,8 +16,8 @@
 // CTAs that start late (their SM still held by the previous kernel) or run
 // slow take fewer tiles and the grid ends together.  The producer hands each
 // chunk's tile range to the MMA and epilogue warps through a small shared-
-// memory ring; the last CTA to finish resets the counters for the next
-// launch.  Q is reloaded only at row changes.
+// memory ring; the last producer to run out of chunks resets the counters
+// for the next launch.  Q is reloaded only at row changes.
 //
 // Two CTAs per SM (two independent pipelines per SM overlap each other's
 // latencies), 6 warps each, warp-specialised:
@@ -337,6 +337,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       cb = __shfl_sync(0xffffffffu, nb, 0);
       ce = __shfl_sync(0xffffffffu, ne, 0);
     }
+    // This producer makes no more claims.  The last one of the grid to get
+    // here resets both counters for the next launch on this workspace (which
+    // starts only after this grid has completed): off the consumers' path,
+    // which still drain the last tiles.
+    if (lane == 0 && nchunks > 0 &&
+        atomicAdd(p.status + kHdrScoreDone, 1) == static_cast<int>(gridDim.x) - 1) {
+      *reinterpret_cast<volatile int*>(claim_ctr) = 0;
+      *reinterpret_cast<volatile int*>(p.status + kHdrScoreDone) = 0;
+    }
     // Never leave with a TMA in flight: wait for the latest fill of every
     // slot (each earlier fill of a slot was consumed, hence complete).
     if (lane == 0) {
@@ -505,16 +514,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(s.tmem_base, kTmemCols);
-  }
-  if (nchunks > 0 && tid == 0) {
-    // Every producer of this CTA has made its last claim (its claims returned
-    // before the barrier above).  The last CTA to get here resets both
-    // counters for the next launch on this workspace, which starts only
-    // after this grid has completed.
-    if (atomicAdd(p.status + kHdrScoreDone, 1) == static_cast<int>(gridDim.x) - 1) {
-      atomicExch(claim_ctr, 0);
-      atomicExch(p.status + kHdrScoreDone, 0);
-    }
   }
 }
 

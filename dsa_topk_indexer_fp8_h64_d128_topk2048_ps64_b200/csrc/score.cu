@@ -82,6 +82,7 @@ constexpr int kChunkSlots = 4;  // chunk ranges in flight from the producer to t
 constexpr int kDynPercent = 25;  // default share of the tile sequence dealt out in chunks,
 constexpr int kDynPerCta = 8;    // capped at this many tiles per CTA
 constexpr int kDynChunk = 4;     // default tiles per chunk
+constexpr int kDynMinPerCta = 8; // chunks only when the sequence has this many tiles per CTA
 
 int env_int_or(const char* name, int dflt) {
   const char* v = getenv(name);
@@ -92,7 +93,6 @@ struct ScoreSmem {
   uint8_t k[kStages][2 * kPageKBytes];  // 1024-B aligned stages, SW128 K-major
   uint8_t q[2][kQBytes];                // SW128 K-major, N = 64 heads
   float scale[kScaleSlots][kTileTok];
-  int2 chunk[kChunkSlots];              // tile range [x, y) of a chunk; x < 0: no more work
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t sfull[kScaleSlots];
@@ -101,13 +101,15 @@ struct ScoreSmem {
   uint64_t qempty[2];
   uint64_t tfull[kAccs];
   uint64_t tempty[kAccs];
-  uint64_t cfull[kChunkSlots];
-  uint64_t cempty[kChunkSlots];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
   int warp_sums[kThreads / 32];
   int row_start[kMaxRowsPerLaunch + 1];
+  // Chunked kernel only: the ring of chunk ranges [x, y) (x < 0: no more work).
+  uint64_t cfull[kChunkSlots];
+  uint64_t cempty[kChunkSlots];
+  int2 chunk[kChunkSlots];
 };
 
 constexpr int kSmemBytes = static_cast<int>(sizeof(ScoreSmem)) + 1024;
@@ -170,6 +172,11 @@ struct ChunkRing {
   uint32_t phase = 0;
 };
 
+// kChunked: the tail of the sequence dealt out in chunks (see the top of the
+// file); without it every CTA takes one static slice and none of the chunk
+// machinery (ring barriers, counters) is compiled in: small launches, where
+// that machinery's set-up sits on the critical path, use this form.
+template <bool kChunked>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     score_kernel(const __grid_constant__ CUtensorMap tmap_q,
                  const __grid_constant__ CUtensorMap tmap_k,
@@ -200,9 +207,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       mbar_init(&s.tfull[i], 1);
       mbar_init(&s.tempty[i], kEpiThreads / 32);
     }
-    for (int i = 0; i < kChunkSlots; ++i) {
-      mbar_init(&s.cfull[i], 1);
-      mbar_init(&s.cempty[i], 1 + kEpiThreads / 32);  // the MMA issuer + the epilogue warps
+    if constexpr (kChunked) {
+      for (int i = 0; i < kChunkSlots; ++i) {
+        mbar_init(&s.cfull[i], 1);
+        mbar_init(&s.cempty[i], 1 + kEpiThreads / 32);  // the MMA issuer + the epilogue warps
+      }
     }
     mbar_init(&s.drain, 1);
     s.abort = 0;
@@ -227,17 +236,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const int* rs = s.row_start;
   const int T = rs[p.rows];
   // Tiles dealt out in chunks: enough to absorb CTAs that start late or run
-  // slow (a few tiles each), not a share that grows with the sequence.
-  const int D = static_cast<int>(min(static_cast<long long>(T) * min(100, max(0, p.dyn_pct)) / 100,
-                                     static_cast<long long>(gridDim.x) * max(0, p.dyn_per_cta)));
+  // slow (a few tiles each), not a share that grows with the sequence; none
+  // when the grid has few tiles per CTA (a chunk would then put several
+  // tiles on one CTA that the static slices spread over several).
+  const bool dyn = kChunked && T >= static_cast<int>(gridDim.x) * kDynMinPerCta;
+  const int D = dyn ? static_cast<int>(min(static_cast<long long>(T) * min(100, max(0, p.dyn_pct)) / 100,
+                                           static_cast<long long>(gridDim.x) * max(0, p.dyn_per_cta)))
+                    : 0;
   const int TS = T - D;                           // tiles in static slices
   const int C = max(1, p.chunk);
   const int nchunks = (D + C - 1) / C;
   const int t0 = static_cast<int>((static_cast<long long>(TS) * blockIdx.x) / gridDim.x);
   const int t1 = static_cast<int>((static_cast<long long>(TS) * (blockIdx.x + 1)) / gridDim.x);
   int* const claim_ctr = p.status + kHdrScoreNext;
+  // Chunk ranges go through the shared-memory ring only when chunks exist;
+  // otherwise every role walks its static slice directly.
+  const bool use_ring = kChunked && nchunks > 0;
 
-  if (warp == 0) {
+  if (!use_ring && t0 >= t1) {
+    // No tiles for this CTA and none to claim (small grids leave most CTAs idle).
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     const uint64_t pol_k = l2_policy_evict_first();
     const uint64_t pol_q = l2_policy_evict_last();
@@ -251,20 +269,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     bool claims_left = nchunks > 0;
     int cb = t0, ce = t1;  // the static slice first
     while (ok) {
-      // Publish [cb, ce) (cb < 0: no more work) to the MMA issuer and the epilogue.
-      int good = 1;
-      if (lane == 0) {
-        if (!mbar_wait(&s.cempty[ring.slot], ring.phase ^ 1u, &s.abort, kWaitTimeoutNs)) {
-          good = 0;
-          fail(s, p.status);
-        } else {
-          s.chunk[ring.slot] = make_int2(cb, ce);
-          mbar_arrive(&s.cfull[ring.slot]);
+      if (use_ring) {
+        // Publish [cb, ce) (cb < 0: no more work) to the MMA issuer and the epilogue.
+        int good = 1;
+        if (lane == 0) {
+          if (!mbar_wait(&s.cempty[ring.slot], ring.phase ^ 1u, &s.abort, kWaitTimeoutNs)) {
+            good = 0;
+            fail(s, p.status);
+          } else {
+            s.chunk[ring.slot] = make_int2(cb, ce);
+            mbar_arrive(&s.cfull[ring.slot]);
+          }
         }
+        if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) break;
       }
-      if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
-      good = __shfl_sync(0xffffffffu, good, 0);
-      if (!good || cb < 0) break;
+      if (cb < 0) break;
 
       TileRef nxt = {0, 0, 0, 0};
       if (cb + lane < ce) nxt = resolve_tile(s, p, cb + lane);
@@ -320,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (!g) { ok = false; break; }
         }
       }
+      if (!use_ring) break;  // the static slice was all there is
       // The next chunk, claimed only now that this one's tiles are all
       // issued: the K ring still holds several tiles for the consumers, which
       // covers the claim's latency, and no CTA sits on a chunk it has not
@@ -341,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     // here resets both counters for the next launch on this workspace (which
     // starts only after this grid has completed): off the consumers' path,
     // which still drain the last tiles.
-    if (lane == 0 && nchunks > 0 &&
+    if (kChunked && lane == 0 && nchunks > 0 &&
         atomicAdd(p.status + kHdrScoreDone, 1) == static_cast<int>(gridDim.x) - 1) {
       *reinterpret_cast<volatile int*>(claim_ctr) = 0;
       *reinterpret_cast<volatile int*>(p.status + kHdrScoreDone) = 0;
@@ -373,11 +395,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       uint32_t qf_par[2] = {0u, 0u};
       ChunkRing ring;
       bool ok = true;
-      while (ok) {
-        if (!mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
-        const int2 ch = s.chunk[ring.slot];
-        mbar_arrive(&s.cempty[ring.slot]);
-        if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+      bool more = true;  // without the ring: the static slice, once
+      while (ok && more) {
+        int2 ch = make_int2(t0, t1);
+        if (use_ring) {
+          if (!mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs)) { fail(s, p.status); break; }
+          ch = s.chunk[ring.slot];
+          mbar_arrive(&s.cempty[ring.slot]);
+          if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+        } else {
+          more = false;
+        }
         if (ch.x < 0) break;
         if (ch.x >= ch.y) continue;
         Cursor c;
@@ -422,16 +450,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     uint32_t* hist_g = nullptr;
     ChunkRing ring;
     bool ok = true;
-    while (ok) {
-      // Waits are decided warp-wide: the warp runs warp-collective steps below.
-      if (!__all_sync(0xffffffffu, mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs))) {
-        fail(s, p.status);
-        break;
+    bool more = true;  // without the ring: the static slice, once
+    while (ok && more) {
+      int2 ch = make_int2(t0, t1);
+      if (use_ring) {
+        // Waits are decided warp-wide: the warp runs warp-collective steps below.
+        if (!__all_sync(0xffffffffu, mbar_wait(&s.cfull[ring.slot], ring.phase, &s.abort, kWaitTimeoutNs))) {
+          fail(s, p.status);
+          break;
+        }
+        ch = s.chunk[ring.slot];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s.cempty[ring.slot]);
+        if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
+      } else {
+        more = false;
       }
-      const int2 ch = s.chunk[ring.slot];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s.cempty[ring.slot]);
-      if (++ring.slot == kChunkSlots) { ring.slot = 0; ring.phase ^= 1u; }
       if (ch.x < 0) break;
       if (ch.x >= ch.y) continue;
       Cursor c;
@@ -528,8 +562,10 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   cudaError_t e0 = cudaGetDevice(&dev);
   if (e0 != cudaSuccess) return e0;
   if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(score_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          kSmemBytes);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(score_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
@@ -564,7 +600,13 @@ cudaError_t launch_score(const ScoreLaunch& lp, const CUtensorMap& tmap_q, const
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return launch_kernel(cfg, score_kernel, tmap_q, tmap_k, tmap_s, p);
+  // The chunked form only when the launch can hold enough tiles per CTA for
+  // chunks to be dealt out (the kernel checks the true count); the tile count
+  // is bounded by rows x tiles of a full block-table row.
+  const long long tiles_max = static_cast<long long>(lp.rows) * ((static_cast<long long>(lp.max_pages) + 1) / 2);
+  const bool chunked = dyn_pct > 0 && dyn_per_cta > 0 &&
+                       tiles_max >= static_cast<long long>(cfg.gridDim.x) * kDynMinPerCta;
+  return launch_kernel(cfg, chunked ? score_kernel<true> : score_kernel<false>, tmap_q, tmap_k, tmap_s, p);
 }
 
 }  // namespace dsai
